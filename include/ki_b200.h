@@ -1,0 +1,186 @@
+/*
+ * ki_b200.h -- C ABI of libki_b200.so: device-wide primitives for NVIDIA B200 (sm_100a) with the
+ * semantics of epilliat/KernelIntrinsics.jl v0.1.6 and the Julia Base operations its intrinsics
+ * are used to build.
+ *
+ * Conventions
+ *   - Every pointer argument named d_* or documented as "device" is a device pointer on the
+ *     context's device; sizes are in elements unless the name says bytes.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream).  All calls are
+ *     stream-ordered and asynchronous; none synchronises unless documented.
+ *   - Every call returns a ki_status.  Errors detected on the device (a bounded wait that ran out)
+ *     are latched in a device status word and reported by ki_ctx_check().
+ *   - No C++ exception crosses this boundary.  No call allocates after the context's scratch has
+ *     grown to the largest problem seen (scratch grows on first use of a size).
+ *   - One context per (device, host thread).  Calls of the same operation through one context
+ *     must be ordered on one stream; they share that operation's scratch.
+ *
+ * Reference interfaces replaced (file:line in the reference project):
+ *   the reference's plugin boundary is a set of Julia stubs that each GPU backend overrides
+ *   (src/scopes_orderings.jl:151-154, src/warp.jl:111-112, src/vectorization.jl:426-448,
+ *   src/KernelIntrinsics.jl:19-21; CUDA overrides in the ext/CUDA directory).  Those run per thread inside a
+ *   user kernel; this ABI exposes the device-wide operations built from them, plus one entry per
+ *   intrinsic family that runs it over whole warps of an array so hosts can test it.
+ */
+#ifndef KI_B200_H
+#define KI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ki_ctx ki_ctx;
+
+typedef enum ki_status {
+    KI_OK = 0,
+    KI_ERR_ARG = 1,         /* invalid argument (the reference raises ArgumentError) */
+    KI_ERR_CUDA = 2,        /* a CUDA runtime call failed; see ki_last_error_string */
+    KI_ERR_TIMEOUT = 3,     /* a bounded device-side wait ran out (lookback flag, mbarrier) */
+    KI_ERR_UNSUPPORTED = 4, /* device is not sm_100 / feature not available */
+    KI_ERR_NOMEM = 5        /* scratch allocation failed */
+} ki_status;
+
+/* Scopes and orderings: src/scopes_orderings.jl:13-120 (Workgroup/Device/System;
+ * Weak/Volatile/Relaxed/Acquire/Release/AcqRel/SeqCst). */
+typedef enum { KI_SCOPE_DEFAULT = 0, KI_SCOPE_WORKGROUP = 1, KI_SCOPE_DEVICE = 2, KI_SCOPE_SYSTEM = 3 } ki_scope;
+typedef enum {
+    KI_ORDER_DEFAULT = 0,
+    KI_ORDER_WEAK = 1,
+    KI_ORDER_VOLATILE = 2,
+    KI_ORDER_RELAXED = 3,
+    KI_ORDER_ACQUIRE = 4,
+    KI_ORDER_RELEASE = 5,
+    KI_ORDER_ACQREL = 6,
+    KI_ORDER_SEQCST = 7
+} ki_order;
+
+/* Shuffle directions (src/warp.jl:16-64) and vote modes (src/warp.jl:66-106). */
+typedef enum { KI_SHFL_UP = 0, KI_SHFL_DOWN = 1, KI_SHFL_XOR = 2, KI_SHFL_IDX = 3 } ki_dir;
+typedef enum { KI_VOTE_ALL = 0, KI_VOTE_ANY = 1, KI_VOTE_UNI = 2, KI_VOTE_BALLOT = 3 } ki_mode;
+
+/* Element types and binary operators for the warp-level entry points. */
+typedef enum {
+    KI_I8 = 0, KI_U8 = 1, KI_I16 = 2, KI_U16 = 3, KI_I32 = 4, KI_U32 = 5,
+    KI_I64 = 6, KI_U64 = 7, KI_F32 = 8, KI_F64 = 9
+} ki_dtype;
+typedef enum { KI_OP_ADD = 0, KI_OP_MAX = 1, KI_OP_MIN = 2, KI_OP_OR = 3, KI_OP_AND = 4, KI_OP_XOR = 5 } ki_op;
+
+/* ---- library / context ------------------------------------------------------------------- */
+
+int ki_version(void);
+const char* ki_status_string(int status);
+
+/* Device queries (src/device.jl:1-19, ext/CUDA/device.jl:4-13, get_warpsize
+ * src/KernelIntrinsics.jl:19).  Devices are 0-based here; the Julia/Python mirrors are 1-based. */
+int ki_device_count(int* count);
+int ki_device_info(int device, int* sm_count, int* warp_size, int* cc_major, int* cc_minor);
+
+int ki_ctx_create(int device, ki_ctx** out);
+int ki_ctx_destroy(ki_ctx* ctx);
+const char* ki_last_error_string(const ki_ctx* ctx);
+/* Synchronises `stream`, returns KI_ERR_TIMEOUT if any device-side wait of this context ran out
+ * since the last check (and clears the latch), KI_ERR_CUDA on an asynchronous CUDA error. */
+int ki_ctx_check(ki_ctx* ctx, void* stream);
+/* Limit of every device-side wait of this context (default 2 s). */
+int ki_ctx_set_wait_timeout_ns(ki_ctx* ctx, uint64_t ns);
+
+/* ---- (a1/a2) vectorised copy: vload_multi / vstore_multi! over a whole range --------------
+ * Replaces: src/vectorization.jl:306-420 (patterns, vload_multi, vstore_multi!),
+ * ext/CUDA/vectorization.jl:5-27 (_vload_batch, _vstore_batch!, _vload_norebase, _vstore_norebase!).
+ * Semantics of copyto!(dst, src) on nbytes bytes; any byte alignment of dst and src.
+ * dst and src must not overlap (KI_ERR_ARG). */
+int ki_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream);
+
+/* ---- (a3) grid-wide reduce (@warpfold, src/warp.jl:273-282) ---------------------------------
+ * sum(x) of n Float32 values, accumulated in Float64 across threads; writes the Float32 result to
+ * d_out_f32 and/or the Float64 result to d_out_f64 (either may be NULL, not both).  n == 0 gives 0.
+ * Deterministic: the same n and device give the same bits on every call. */
+int ki_reduce_sum_f32(ki_ctx* ctx, const float* d_x, size_t n, float* d_out_f32, double* d_out_f64,
+                      void* stream);
+/* sum of Int64 with two's-complement wrap-around (the shard total of the sharded scan). */
+int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out, void* stream);
+
+/* ---- (a4/a5) single-pass decoupled-lookback inclusive scan ----------------------------------
+ * Replaces: @warpreduce (src/warp.jl:226-237) for the in-warp scan, @access / @fence
+ * (src/macros.jl:198-282, ext/CUDA/scopes_ordering.jl:89-193) for the tile flags.
+ * out[i] = seed + in[0] + ... + in[i] with Int64 wrap-around (Base.cumsum; seed = 0).
+ * in == out is allowed (in place).  Tile flags use st.release.gpu / ld.acquire.gpu; waits are
+ * bounded by the context's timeout. */
+int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
+                          void* stream);
+
+/* ---- (a6) order-preserving stream compaction (@vote Ballot, ext/CUDA/shuffle_vote.jl:23-34) --
+ * Keeps x[i] > threshold in order: out_vals[j] = x[i_j], out_idx[j] = i_j + index_base (Int32;
+ * index_base = 1 gives findall's 1-based indices).  *d_count (device, uint64) receives the count.
+ * out_vals and out_idx must hold n entries (either may be NULL).  Requires
+ * index_base + n - 1 <= INT32_MAX and index_base >= INT32_MIN. */
+int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float threshold, float* d_out_vals,
+                      int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream);
+
+/* ---- (a8) fp8 e4m3 GEMM on tcgen05 / TMEM ---------------------------------------------------
+ * No counterpart in the reference.  C = (scale_a * scale_b) * A * B with A: M x K row-major e4m3,
+ * B: K x N row-major e4m3, C: M x N row-major Float32, Float32 accumulation.
+ * M, N multiples of 128 and 256, K a multiple of 128, pointers 16-byte aligned (KI_ERR_ARG). */
+int ki_gemm_e4m3_f32(ki_ctx* ctx, const uint8_t* d_A, const uint8_t* d_B, float* d_C, int M, int N, int K,
+                     float scale_a, float scale_b, void* stream);
+
+/* ---- warp-level intrinsics over whole warps of an array -------------------------------------
+ * Element i of the array is lane i % 32 of warp i / 32; n must be a multiple of 32.           */
+
+/* @shfl (src/warp.jl:114-192): any element size 1..64 bytes (moved as 32-bit words, the
+ * reference's _shfl_recurse decomposition).  `src` is the offset (Up/Down), the lane mask (Xor)
+ * or the 0-BASED source lane (Idx). */
+int ki_warp_shfl(ki_ctx* ctx, int dir, const void* d_src, void* d_dst, size_t elem_bytes, size_t n, int src,
+                 void* stream);
+/* @warpreduce (src/warp.jl:226-237): inclusive scan per warp with Up shuffles. */
+int ki_warp_reduce(ki_ctx* ctx, int op, int dtype, const void* d_src, void* d_dst, size_t n, void* stream);
+/* @warpfold (src/warp.jl:273-282).  form 0: xor butterfly, every lane holds the total;
+ * form 1: the reference's Down fold exactly (lane 1 holds the total, others partial folds). */
+int ki_warp_fold(ki_ctx* ctx, int op, int dtype, int form, const void* d_src, void* d_dst, size_t n,
+                 void* stream);
+/* @vote (src/warp.jl:311-315; ext/CUDA/shuffle_vote.jl:23-34): d_pred is one byte per lane
+ * (nonzero = true); d_out is one uint32 per lane: 0/1 for All/AnyLane/Uni, the mask for Ballot. */
+int ki_warp_vote(ki_ctx* ctx, int mode, const uint8_t* d_pred, uint32_t* d_out, size_t n, void* stream);
+
+/* vload / vstore! (src/vectorization.jl:135-300) run by one device thread.
+ * rebase != 0: idx is a 0-based block index (elements idx*nitem ..); otherwise a 0-based element
+ * index.  elem_bytes 1,2,4,8,16 use vector accesses with the runtime alignment check and the
+ * generate_partN patterns; other sizes use the scalar path.  nitem in {1,2,4,8,16}. */
+int ki_vload(ki_ctx* ctx, const void* d_a, size_t elem_bytes, int64_t idx, int nitem, int rebase, void* d_out,
+             void* stream);
+int ki_vstore(ki_ctx* ctx, void* d_a, size_t elem_bytes, int64_t idx, int nitem, int rebase,
+              const void* d_values, void* stream);
+
+/* @access / @fence (src/macros.jl:198-282; ext/CUDA/scopes_ordering.jl:29-193), one device thread:
+ * stores *d_value into *d_slot with (scope, store_order), issues fence(fence_scope, fence_order)
+ * (KI_SCOPE_DEFAULT / KI_ORDER_DEFAULT give @fence's defaults, Device and AcqRel), then loads
+ * *d_slot with (scope, load_order) into *d_readback.  Orderings default as @access does (Release
+ * for the store, Acquire for the load).  Invalid combinations give KI_ERR_ARG under the
+ * reference's validation rules.  dtype: any ki_dtype. */
+int ki_access_roundtrip(ki_ctx* ctx, int dtype, int scope, int store_order, int load_order, int fence_scope,
+                        int fence_order, void* d_slot, const void* d_value, void* d_readback, void* stream);
+/* Release/acquire message passing: block 0 writes `payload` to d_data[0] and release-stores 1 to
+ * *d_flag (only when produce != 0); blocks 1..nblocks-1 spin with bounded acquire loads until the
+ * flag is 1 and copy d_data[0] into d_seen[block].  A consumer whose wait runs out (produce == 0,
+ * or timeout_ns elapsed) writes -1 and latches KI_ERR_TIMEOUT for ki_ctx_check. */
+int ki_flag_message_pass(ki_ctx* ctx, int64_t* d_data, uint32_t* d_flag, int64_t* d_seen, int nblocks,
+                         int64_t payload, int produce, uint64_t timeout_ns, void* stream);
+
+/* ---- synthetic input generators (bit-identical to the host generators) ---------------------
+ * Element i of stream `seed` is splitmix64's (i+1)-th output: mix64(seed + (i+1)*0x9E3779B97F4A7C15). */
+int ki_fill_uniform_f32(ki_ctx* ctx, uint64_t seed, float* d_out, size_t n, void* stream);   /* (r>>40)*2^-24 */
+int ki_fill_int_range_i64(ki_ctx* ctx, uint64_t seed, int64_t lo, int64_t hi, int64_t* d_out, size_t n,
+                          void* stream);                                                         /* r%(hi-lo+1)+lo */
+int ki_fill_bytes(ki_ctx* ctx, uint64_t seed, uint8_t* d_out, size_t n, void* stream);       /* byte i%8 of word i/8 */
+int ki_fill_normal_f32(ki_ctx* ctx, uint64_t seed, float* d_out, size_t n, void* stream);    /* Box-Muller */
+int ki_fill_e4m3_uniform(ki_ctx* ctx, uint64_t seed, float scale, uint8_t* d_out, size_t n,
+                         void* stream);                                          /* e4m3((2u-1)*scale) */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KI_B200_H */

@@ -1,0 +1,103 @@
+"""GPU: stream compaction (filter / findall) and the device generators."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("n", [1, 2, 31, 32, 33, 4095, 4096, 4097, 100003, (1 << 20) + 1])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_compact_vs_oracle(KI, oracle, dev, n, offset):
+    import torch
+
+    base = torch.empty(n + offset, dtype=torch.float32, device=dev)
+    KI.fill_normal(base, seed=4)
+    x = base[offset:]
+    host = x.cpu().numpy()
+    for index_base in (1, 0, 1000):
+        vals, idx, cnt = KI.vote_compact(x, 0.5, index_base=index_base)
+        KI.context(0).check()
+        rv, ri = oracle.filter_gt_f32(host, 0.5, index_base=index_base)
+        assert cnt.item() == rv.size
+        assert np.array_equal(vals.cpu().numpy(), rv)
+        assert np.array_equal(idx.cpu().numpy(), ri)
+
+
+def test_compact_edge_values(KI, oracle, dev):
+    import torch
+
+    host = np.array([0.5, np.nextafter(np.float32(0.5), np.float32(1)), np.nan, np.inf, -np.inf, 0.49999997, 7.0]
+                    * 1000, dtype=np.float32)
+    x = torch.from_numpy(host).to(dev)
+    vals, idx, cnt = KI.vote_compact(x, 0.5)
+    rv, ri = oracle.filter_gt_f32(host, 0.5)
+    assert np.array_equal(vals.cpu().numpy(), rv) and np.array_equal(idx.cpu().numpy(), ri)
+    e, ei, ec = KI.vote_compact(torch.empty(0, dtype=torch.float32, device=dev), 0.5)
+    assert ec.item() == 0 and e.numel() == 0
+    none = torch.zeros(10000, dtype=torch.float32, device=dev)
+    assert KI.vote_compact(none, 0.5)[2].item() == 0
+    allk = torch.ones(10000, dtype=torch.float32, device=dev)
+    v, i, c = KI.vote_compact(allk, 0.5)
+    assert c.item() == 10000 and torch.equal(i.cpu(), torch.arange(1, 10001, dtype=torch.int32))
+
+
+def test_compact_rejects_index_overflow(KI, dev):
+    import torch
+
+    x = torch.zeros(16, dtype=torch.float32, device=dev)
+    with pytest.raises(KI.KIArgumentError):
+        KI.vote_compact(x, 0.5, index_base=2**31 - 4)
+
+
+def test_compact_config_size(KI, dev):
+    """n = 2^28 N(0,1), x > 0.5: equal to torch's nonzero on the same data; k near 0.30854 n."""
+    import torch
+
+    n = 1 << 28
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    KI.fill_normal(x, seed=4)
+    vals, idx, cnt = KI.vote_compact(x, 0.5)
+    KI.context(0).check()
+    keep = torch.nonzero(x > 0.5).flatten()
+    k = cnt.item()
+    assert k == keep.numel()
+    assert abs(k / n - 0.308538) < 1e-3
+    assert torch.equal(idx.to(torch.int64) - 1, keep)
+    assert torch.equal(vals, x[keep])
+    del x, vals, idx, keep
+    torch.cuda.empty_cache()
+
+
+def test_generators_match_host(KI, oracle, dev):
+    import torch
+
+    n = (1 << 20) + 13
+    u = torch.empty(n, dtype=torch.float32, device=dev)
+    KI.fill_uniform(u, seed=1)
+    assert np.array_equal(u.cpu().numpy(), oracle.gen_uniform_f32(1, n))
+    i = torch.empty(n, dtype=torch.int64, device=dev)
+    KI.fill_int_range(i, seed=3, lo=-1000, hi=1000)
+    assert np.array_equal(i.cpu().numpy(), oracle.gen_int_range_i64(3, -1000, 1000, n))
+    b = torch.empty(n, dtype=torch.uint8, device=dev)
+    KI.fill_bytes(b, seed=2)
+    assert np.array_equal(b.cpu().numpy(), oracle.gen_bytes(2, n))
+    bo = torch.empty(n + 3, dtype=torch.uint8, device=dev)[3:]  # unaligned start
+    KI.fill_bytes(bo, seed=2)
+    assert np.array_equal(bo.cpu().numpy(), oracle.gen_bytes(2, n))
+    q = torch.empty(n, dtype=torch.uint8, device=dev)
+    KI.fill_e4m3_uniform(q, seed=5, scale=112.0)
+    assert np.array_equal(q.cpu().numpy(), oracle.gen_e4m3_uniform(5, 112.0, n))
+
+
+def test_normal_generator_distribution(KI, dev):
+    import torch
+
+    n = 1 << 24
+    z = torch.empty(n, dtype=torch.float32, device=dev)
+    KI.fill_normal(z, seed=4)
+    zd = z.double()
+    assert abs(zd.mean().item()) < 2e-3 and abs(zd.std().item() - 1) < 2e-3
+    assert abs((z > 0.5).double().mean().item() - 0.308538) < 1e-3
+    assert torch.isfinite(z).all()

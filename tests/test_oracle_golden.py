@@ -1,0 +1,141 @@
+"""CPU: the oracle reproduces the reference's own known answers and Julia Base semantics."""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+import pytest
+
+
+def test_shfl_golden(oracle, golden):
+    for c in golden["shfl"]:
+        got = oracle.shfl(c["dir"], c["input"], c["arg"])
+        assert got == c["expected"], c["name"]
+
+
+def test_shfl_struct_golden(oracle, golden):
+    # whole values move together, so shuffling indices is enough for the oracle
+    for c in golden["shfl_struct"]:
+        got = oracle.shfl(c["dir"], [tuple(v) for v in c["input"]], c["arg"])
+        assert [list(v) for v in got] == c["expected"], c["name"]
+
+
+def test_warpreduce_golden(oracle, golden):
+    for c in golden["warp"]:
+        if "expected" in c:
+            got = oracle.warpreduce(c["input"], lambda a, b: a + b)
+            assert got == c["expected"], c["name"]
+        else:
+            got = oracle.warpfold_down(c["input"], lambda a, b: a + b)
+            assert got[0] == c["expected_lane1"], c["name"]
+
+
+def test_warpfold_down_only_lane1_is_total(oracle):
+    v = list(range(1, 33))
+    got = oracle.warpfold_down(v, lambda a, b: a + b)
+    assert got[0] == 528
+    assert got[31] != 528  # the top lanes re-add their own value (src/warp.jl:35-37)
+
+
+def test_vote_golden(oracle, golden):
+    for c in golden["vote"]:
+        preds = [x > c["threshold"] for x in c["input"]]
+        got = oracle.vote(c["mode"], preds)
+        assert [bool(g) for g in got] == c["expected"], c["name"]
+    assert oracle.vote("ballot", [True] * 32)[0] == 0xFFFFFFFF
+    assert oracle.vote("ballot", [l % 2 == 1 for l in range(32)])[0] == 0xAAAAAAAA
+
+
+def test_generate_partN_golden(oracle, golden):
+    for p in golden["patterns"]:
+        assert oracle.generate_partN(p["N"])[p["residue"]] == tuple(p["pattern"])
+    for N in (1, 2, 4, 8, 16, 32):
+        for r, pat in enumerate(oracle.generate_partN(N)):
+            assert sum(pat) == N
+            pos = r
+            for piece in pat:
+                assert pos % piece == 0 or piece == 1  # naturally aligned
+                if r:
+                    assert piece <= max(N // 2, 1)
+                pos = (pos + piece) % N
+
+
+def test_generate_partN_matches_package(oracle):
+    import kernelintrinsics as KI
+
+    for N in (1, 2, 4, 8, 16, 64):
+        assert KI.generate_partN(N) == oracle.generate_partN(N)
+
+
+def test_vload_multi_golden(oracle, golden):
+    for c in golden["vector"]:
+        if c["op"] != "vload" or c["rebase"] or c["nitem"] != 16:
+            continue
+        pieces = oracle.vload_multi_pieces(0, c["index_1based"], 16)
+        elems = [e for start, ln in pieces for e in range(start, start + ln)]
+        assert [c["array"][e - 1] for e in elems] == c["expected"], c["name"]
+
+
+def test_generators_known_answer(oracle):
+    # splitmix64 reference value: the first output of a generator seeded with 0
+    assert oracle.rand64(0, 0) == 0xE220A8397B1DCDAF
+    x = oracle.gen_uniform_f32(1, 1 << 16)
+    assert x.min() >= 0 and x.max() < 1
+    assert np.all(x * 2**24 == np.floor(x * 2**24))
+    y = oracle.gen_int_range_i64(3, -1000, 1000, 1 << 16)
+    assert y.min() == -1000 and y.max() == 1000
+    b = oracle.gen_bytes(2, 64)
+    w = oracle.rand64(2, 0)
+    assert bytes(b[:8]) == struct.pack("<Q", w)
+
+
+def test_e4m3_codec(oracle):
+    t = oracle.e4m3_decode_table()
+    assert t[0x7E] == 448 and np.isnan(t[0x7F]) and t[0x01] == 2.0**-9 and t[0x08] == 2.0**-6
+    for i in range(256):
+        if i in (0x7F, 0xFF):
+            continue
+        assert oracle.e4m3_encode(t[i]) == i
+    assert oracle.e4m3_encode(1000.0) == 0x7E and oracle.e4m3_encode(-1000.0) == 0xFE
+    assert oracle.e4m3_encode(1.0625) == oracle.e4m3_encode(1.0)      # tie to even
+    assert oracle.e4m3_encode(1.1875) == oracle.e4m3_encode(1.25)     # tie to even
+
+
+def test_e4m3_generator_range(oracle):
+    q = oracle.gen_e4m3_uniform(5, 112.0, 1 << 16)
+    v = oracle.e4m3_decode_table()[q]
+    assert np.abs(v).max() <= 112 and np.isfinite(v).all()
+
+
+def test_base_semantics_sum(oracle, base_semantics):
+    s = oracle.sum_f32(base_semantics["sum_x"])
+    assert abs(s - base_semantics["sum_f64"][0]) <= 1e-12 * abs(s)
+
+
+def test_base_semantics_cumsum(oracle, base_semantics):
+    assert np.array_equal(oracle.cumsum_i64(base_semantics["scan_x"]), base_semantics["scan_y"])
+    assert np.array_equal(oracle.cumsum_i64(base_semantics["wrap_x"]), base_semantics["wrap_y"])
+    for nt in (1, 3, 8):
+        assert np.array_equal(oracle.cumsum_i64(base_semantics["scan_x"], nthreads=nt), base_semantics["scan_y"])
+
+
+def test_base_semantics_filter(oracle, base_semantics):
+    v, i = oracle.filter_gt_f32(base_semantics["filt_x"], 0.5)
+    assert np.array_equal(v, base_semantics["filt_vals"])
+    assert np.array_equal(i, base_semantics["filt_idx1"])
+    v0, i0 = oracle.filter_gt_f32(np.zeros(0, np.float32), 0.5)
+    assert v0.size == 0 and i0.size == 0
+
+
+def test_copy_and_gemm_oracle(oracle):
+    src = oracle.gen_bytes(9, 1000)
+    dst = np.zeros(1000, np.uint8)
+    oracle.copy_bytes(dst, src)
+    assert np.array_equal(src, dst)
+    A = oracle.gen_e4m3_uniform(5, 112.0, 64 * 48).reshape(64, 48)
+    B = oracle.gen_e4m3_uniform(6, 112.0, 48 * 40).reshape(48, 40)
+    lut = oracle.e4m3_decode_table().astype(np.float64)
+    ref = lut[A] @ lut[B]
+    got = oracle.gemm_e4m3_rows(A, B, 0, 64)
+    assert np.allclose(got, ref, rtol=0, atol=1e-9)
+    assert np.allclose(oracle.gemm_e4m3_rows(A, B, 10, 20, scale=0.5), 0.5 * ref[10:20])

@@ -284,7 +284,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t ph = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
-            if (!wait_bar(tfull0 + 8 * acc, ph, abort, status, timeout_ns)) break;
+            int ok = 0;
+            if (lane == 0) ok = wait_bar(tfull0 + 8 * acc, ph, abort, status, timeout_ns) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);  // one decision for the whole warp
+            if (!ok) break;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < BN / EPI_COLS; ++c) {
@@ -328,6 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
+        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }

@@ -112,6 +112,18 @@ int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out,
 int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
                           void* stream);
 
+/* Allocation-free scan.  No counterpart in the reference.
+ * For callers that cannot allocate device memory: code running while a CUDA graph is captured,
+ * hosts whose device memory belongs to another allocator, loops that forbid allocation after
+ * start-up.  Same result as ki_scan_inclusive_i64, but needs no context and calls no cudaMalloc,
+ * cudaFree or allocating routine: its tile-status scratch is a static device array sized for
+ * n <= KI_SCAN_NOALLOC_MAX_N (about 1.5 MiB, held by every GPU that loads the library until exit).
+ * n beyond that returns KI_ERR_ARG.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current): make it before any stream capture.
+ * Every call shares the array; calls that overlap on the GPU race.  Uses the current device. */
+#define KI_SCAN_NOALLOC_MAX_N (1ull << 28)
+int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed, void* stream);
+
 /* ---- (a6) order-preserving stream compaction (@vote Ballot, ext/CUDA/shuffle_vote.jl:23-34) --
  * Keeps x[i] > threshold in order: out_vals[j] = x[i_j], out_idx[j] = i_j + index_base (Int32;
  * index_base = 1 gives findall's 1-based indices).  *d_count (device, uint64) receives the count.

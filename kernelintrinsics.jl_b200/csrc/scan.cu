@@ -171,3 +171,85 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     scan_i64_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
     return ki::check_launch(ctx, "scan_i64_kernel launch");
 }
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is being captured, hosts
+// whose memory is owned by another allocator (a Julia or Python pool that must not be bypassed), or
+// real-time loops that forbid allocation after start-up.  ki_scan_inclusive_i64_noalloc runs the
+// same kernel as ki_scan_inclusive_i64 but takes its tile-status scratch from the file-scope array
+// below instead of a context, so it needs no context and allocates nothing.
+//
+// The array is sized for KI_SCAN_NOALLOC_MAX_N elements (65,536 tiles: a 256-byte header plus three
+// 8-byte words per tile, about 1.5 MiB).  Every GPU that loads this library holds it until the
+// process exits.  In host code the array's name is only a host-side stand-in, so its device address
+// is looked up once per device with cudaGetSymbolAddress (with that device current) and cached; the
+// first call on each device does this set-up and must therefore come before any stream capture.
+// All calls share the array and it keeps the last call's contents: each call clears the ticket, the
+// status word and the tile flags (cudaMemsetAsync on the cached address) before its launch, and
+// calls that overlap on the GPU (different streams, or several host threads) race on it.
+// A bounded wait that runs out is latched in the array's status word and not reported; use the
+// context API where timeout reporting is needed.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocTiles = (KI_SCAN_NOALLOC_MAX_N + kTile - 1) / kTile;
+constexpr size_t kNoAllocHeader = 256;  // ticket at 0, status word at 64
+static __device__ __align__(256) unsigned char g_scan_noalloc_scratch[kNoAllocHeader + kNoAllocTiles * 24];
+
+struct NoAllocDevice {
+    bool ready = false;
+    unsigned char* scratch = nullptr;
+};
+std::mutex g_noalloc_mutex;
+NoAllocDevice g_noalloc_dev[64];
+
+}  // namespace
+
+extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
+                                             void* stream) {
+    if (n == 0) return KI_OK;
+    if (n > (size_t)KI_SCAN_NOALLOC_MAX_N) return KI_ERR_ARG;  // beyond the static scratch
+    if (!d_in || !d_out) return KI_ERR_ARG;
+    if (!ki::aligned(d_in, 8) || !ki::aligned(d_out, 8)) return KI_ERR_ARG;
+    if (d_in != d_out) {
+        const uintptr_t i0 = (uintptr_t)d_in, o0 = (uintptr_t)d_out, nb = n * sizeof(int64_t);
+        if (i0 < o0 + nb && o0 < i0 + nb) return KI_ERR_ARG;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KI_ERR_CUDA;
+    unsigned char* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        NoAllocDevice& d = g_noalloc_dev[dev];
+        if (!d.ready) {
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_scan_noalloc_scratch) != cudaSuccess || !p) return KI_ERR_CUDA;
+            if (cudaFuncSetAttribute(scan_i64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kSmemBytes) != cudaSuccess)
+                return KI_ERR_CUDA;
+            d.scratch = static_cast<unsigned char*>(p);
+            d.ready = true;
+        }
+        scratch = d.scratch;
+    }
+    const size_t ntiles = (n + kTile - 1) / kTile;
+    cudaStream_t s = ki::as_stream(stream);
+    if (cudaMemsetAsync(scratch, 0, kNoAllocHeader + ntiles * sizeof(uint64_t), s) != cudaSuccess)
+        return KI_ERR_CUDA;
+    ScanArgs a;
+    a.in = d_in;
+    a.out = d_out;
+    a.n = n;
+    a.seed = seed;
+    a.st.flags = reinterpret_cast<uint64_t*>(scratch + kNoAllocHeader);
+    a.st.aggs = reinterpret_cast<int64_t*>(scratch + kNoAllocHeader + kNoAllocTiles * 8);
+    a.st.incls = reinterpret_cast<int64_t*>(scratch + kNoAllocHeader + kNoAllocTiles * 16);
+    a.ticket = reinterpret_cast<unsigned long long*>(scratch);
+    a.status = reinterpret_cast<uint32_t*>(scratch + 64);
+    a.timeout_ns = 2000000000ull;
+    a.use_tma = ki::aligned(d_in, 16) && ki::aligned(d_out, 16);
+    scan_i64_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
+    return cudaGetLastError() == cudaSuccess ? KI_OK : KI_ERR_CUDA;
+}

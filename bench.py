@@ -59,7 +59,79 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="", help="comma list of kernels to run under 'kernels'")
+    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm"],
+                   help="run only this kernel, --profile-launches times, on a small case (for ncu)")
+    p.add_argument("--profile-n", type=int, default=0, help="elements (bytes for copy; M=N=K for gemm)")
+    p.add_argument("--profile-launches", type=int, default=3)
     return p.parse_args()
+
+
+def run_profile(args):
+    """A small case of one kernel: 2 warm-up launches, then --profile-launches timed launches."""
+    import torch
+
+    torch.cuda.set_device(0)
+    import kernelintrinsics as KI
+
+    dev = torch.device("cuda", 0)
+    k = args.profile
+    n = args.profile_n
+    if k == "copy":
+        n = n or COPY_BYTES
+        src = torch.empty(n + 16, dtype=torch.uint8, device=dev)
+        KI.fill_bytes(src, seed=2)
+        dst = torch.empty_like(src)
+        fn = lambda: KI.vcopy(dst, src, n, dst_offset=3, src_offset=7)
+        alg = 2 * n
+    elif k == "reduce":
+        n = n or REDUCE_N
+        x = torch.empty(n, dtype=torch.float32, device=dev)
+        KI.fill_uniform(x, seed=1)
+        out = torch.empty((), dtype=torch.float64, device=dev)
+        fn = lambda: KI.warpfold_reduce(x, out_f64=out)
+        alg = 4 * n
+    elif k == "scan":
+        n = n or (1 << 26)
+        x = torch.empty(n, dtype=torch.int64, device=dev)
+        KI.fill_int_range(x, seed=3, lo=-1000, hi=1000)
+        y = torch.empty_like(x)
+        fn = lambda: KI.warpreduce_scan(x, out=y)
+        alg = 16 * n
+    elif k == "compact":
+        n = n or (1 << 26)
+        x = torch.empty(n, dtype=torch.float32, device=dev)
+        KI.fill_normal(x, seed=4)
+        v = torch.empty_like(x)
+        i = torch.empty(n, dtype=torch.int32, device=dev)
+        c = torch.zeros((), dtype=torch.uint64, device=dev)
+        fn = lambda: KI.vote_compact(x, 0.5, out_vals=v, out_idx=i, count=c, trim=False)
+        alg = 4 * n + 8 * int(0.30854 * n)
+    else:
+        n = n or 4096
+        A = torch.empty((n, n), dtype=torch.uint8, device=dev)
+        B = torch.empty((n, n), dtype=torch.uint8, device=dev)
+        KI.fill_e4m3_uniform(A, seed=5, scale=112.0)
+        KI.fill_e4m3_uniform(B, seed=6, scale=112.0)
+        C = torch.empty((n, n), dtype=torch.float32, device=dev)
+        fn = lambda: KI.fp8_gemm(A, B, C)
+        alg = 2 * n ** 3
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.profile_launches):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        ts.append((a, b))
+    torch.cuda.synchronize()
+    KI.context(0).check()
+    ms = statistics.median(a.elapsed_time(b) for a, b in ts)
+    unit = "TFLOP/s" if k == "gemm" else "GB/s"
+    val = alg / (ms * 1e-3) / (1e12 if k == "gemm" else 1e9)
+    print(json.dumps({"profile": k, "n": n, "ms_median": round(ms, 5), "value": round(val, 2), "unit": unit}))
+    return 0
 
 
 # ---------------------------------------------------------------------------------------------
@@ -305,23 +377,32 @@ def bench_reduce(KI, D, steps, warmup, hbm):
 
     dev = torch.device("cuda", D.dev)
     lo, hi = sharded.shard_range(REDUCE_N, D.world, D.rank)
-    x = torch.empty(hi - lo, dtype=torch.float32, device=dev)
-    KI.fill_uniform(x, seed=1)  # shard-local stream; the parity tests check the global one
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    # 8 rotating inputs (8 x 64 MiB at N=1, more than L2): each step reads data that is not in L2.
+    nbuf = max(8, (1 << 29) // max(4 * (hi - lo), 1))
+    xs = [torch.empty(hi - lo, dtype=torch.float32, device=dev) for _ in range(nbuf)]
+    for k, x in enumerate(xs):
+        KI.fill_uniform(x, seed=1 + k)  # shard-local streams; the parity tests check the global one
     stream = torch.cuda.current_stream(dev)
     out = torch.empty((), dtype=torch.float64, device=dev)
-    if D.world == 1:
-        step = lambda: KI.warpfold_reduce(x, out_f64=out)
-    else:
-        step = lambda: sharded.reduce_sharded(x)
-    mean_ms, med_ms = _timed_steps(D, stream, step, steps, warmup, between=lambda: flush.zero_())
+    it = [0]
+
+    def step():
+        x = xs[it[0] % nbuf]
+        it[0] += 1
+        if D.world == 1:
+            KI.warpfold_reduce(x, out_f64=out)
+        else:
+            sharded.reduce_sharded(x)
+
+    mean_ms, med_ms = _timed_steps(D, stream, step, steps, warmup)
     gbs = 4 * REDUCE_N / (mean_ms * 1e-3) / 1e9
     per_gpu = gbs / D.world
-    del x, flush
+    del xs
     torch.cuda.empty_cache()
     return {"workload": f"Float32 sum n=2^24 ({D.world} shard(s))", "value": round(gbs, 2), "unit": "GB/s",
             "ms_per_step": round(mean_ms, 5), "ms_median": round(med_ms, 5),
-            "frac_of_hbm_per_gpu": round(per_gpu / hbm, 4), "l2": "flushed between steps (256 MiB write)",
+            "frac_of_hbm_per_gpu": round(per_gpu / hbm, 4),
+            "l2": f"{nbuf} rotating inputs ({nbuf * 4 * (hi - lo) >> 20} MiB > L2): no step reads cached data",
             "algorithmic_bytes": 4 * REDUCE_N}
 
 
@@ -502,6 +583,8 @@ def run_reference(args, D):
 # ---------------------------------------------------------------------------------------------
 def main():
     args = parse()
+    if args.profile:
+        return run_profile(args)
     D = Dist(args.gpus)
     if args.impl == "reference":
         return run_reference(args, D)

@@ -1,15 +1,18 @@
 // ki/lookback.cuh -- decoupled lookback over per-tile status words, and 1-D TMA bulk helpers.
 //
-// Tile status (one entry per tile, reset to 0 before each call):
-//   flags[t] : 0 = nothing published, 1 = aggregate published (A), 2 = inclusive prefix (P)
-//   aggs[t]  : the tile's own aggregate          (valid once flags[t] >= 1)
-//   incls[t] : inclusive prefix through tile t    (valid once flags[t] == 2)
-// A value is written with a plain store, then the flag with st.release.gpu; readers load the flag
-// with ld.acquire.gpu and then the value with ld.relaxed.gpu.  These are the @access store /
-// load defaults of the reference (src/macros.jl:259-275 -> ext/CUDA/scopes_ordering.jl:89-193).
+// Tile status, one 64-bit word per tile (reset to 0 before each call):
+//   bits 0-1  state: 0 = nothing published, 1 = aggregate published (A), 2 = inclusive prefix (P)
+//   bit  2    wide: the value did not fit and lives in aggs[t] (A) or incls[t] (P)
+//   bits 3-63 the value as a 61-bit two's-complement integer (when not wide)
+// A packed word is published with one st.release.gpu and read with one ld.acquire.gpu, so looking
+// back over a window of 32 tiles costs one round trip to L2.  A value outside the 61-bit range is
+// first written to its side array with a plain store, then the word (state | wide) is published
+// with st.release.gpu; a reader that acquires such a word loads the value with ld.relaxed.gpu.
+// These are the @access store / load defaults of the reference (src/macros.jl:259-275 ->
+// ext/CUDA/scopes_ordering.jl:89-193).
 //
 // Every wait is bounded by %globaltimer: when it runs out the warp latches KI_DEV_TIMEOUT in the
-// context's status word and carries on with what it has, so the grid always finishes.
+// status word it was given and carries on with what it has, so the grid always finishes.
 #pragma once
 
 #include <cstdint>
@@ -17,74 +20,127 @@
 #include "common.cuh"
 #include "intrinsics.cuh"
 
+// Sleep between re-reads of a window that still has unpublished tiles (doubles up to the max).
+#ifndef KI_LOOKBACK_MIN_SLEEP_NS
+#define KI_LOOKBACK_MIN_SLEEP_NS 32
+#endif
+#ifndef KI_LOOKBACK_MAX_SLEEP_NS
+#define KI_LOOKBACK_MAX_SLEEP_NS 512
+#endif
+
 namespace ki {
 
-constexpr uint64_t kFlagNone = 0, kFlagAgg = 1, kFlagPrefix = 2;
+constexpr uint64_t kFlagNone = 0, kFlagAgg = 1, kFlagPrefix = 2, kFlagWide = 4;
 
 struct TileStatus {
-    uint64_t* flags;
+    uint64_t* words;
     int64_t* aggs;
     int64_t* incls;
 };
 
-// Run by all 32 lanes of one warp.  Publishes tile t's aggregate, looks back over predecessors
-// until an inclusive prefix is found, publishes tile t's inclusive prefix and returns the exclusive
-// prefix of tile t (including `seed`).  Sums wrap around (two's complement).
+__device__ __forceinline__ bool fits61(int64_t v) { return v >= -(1ll << 60) && v < (1ll << 60); }
+
+__device__ __forceinline__ void publish(TileStatus st, uint64_t t, uint64_t state, int64_t v) {
+    if (fits61(v)) {
+        store<Order::Release, Scope::Device>(&st.words[t], ((uint64_t)v << 3) | state);
+    } else {
+        (state == kFlagPrefix ? st.incls : st.aggs)[t] = v;
+        store<Order::Release, Scope::Device>(&st.words[t], kFlagWide | state);
+    }
+}
+
+// Run by all 32 lanes of one warp, after publish_aggregate(t).  Looks back over predecessors until
+// an inclusive prefix is found, publishes tile t's inclusive prefix and returns the exclusive prefix
+// of tile t (including `seed`).  Sums wrap around (two's complement).
+//
+// The window is 32*K tiles: lane l reads the K words of tiles end-(l*K) .. end-(l*K+K-1) with
+// independent ld.relaxed.gpu loads, so a whole window costs one round trip (acquire loads would be
+// performed one after another).  Packed words carry their value, so nothing else is read; a wide
+// value is read from its side array after a fence.acq_rel.gpu, which with the relaxed load of its
+// word is the fence form of an acquire (@access Relaxed + @fence).  Throughput of a lookback
+// chain is bounded by window / round trip, hence the wide window.
+//
+// The caller publishes the tile's aggregate first (publish_aggregate), as soon as its data has
+// landed, and may do other work before looking back: a tile's aggregate must never wait behind its
+// owner's other work, or owners end up waiting on one another.
+__device__ __forceinline__ void publish_aggregate(TileStatus st, uint64_t t, int64_t agg, int64_t seed) {
+    if (t == 0) publish(st, 0, kFlagPrefix, wrap_add(seed, agg));
+    else publish(st, t, kFlagAgg, agg);
+}
+
+template <int K>
 __device__ __forceinline__ int64_t decoupled_lookback(TileStatus st, uint64_t t, int64_t agg, int64_t seed,
                                                       uint32_t* status, uint64_t timeout_ns) {
     const unsigned lane = lane0();
-    if (t == 0) {
-        if (lane == 0) {
-            st.incls[0] = wrap_add(seed, agg);
-            store<Order::Release, Scope::Device>(&st.flags[0], kFlagPrefix);
-        }
-        return seed;
-    }
-    if (lane == 0) {
-        st.aggs[t] = agg;
-        store<Order::Release, Scope::Device>(&st.flags[t], kFlagAgg);
-    }
+    if (t == 0) return seed;
     int64_t excl = 0;
-    long long end = (long long)t - 1;  // window = tiles end-31 .. end, lane k looks at end-k
+    long long end = (long long)t - 1;  // nearest tile of the current window
     uint64_t t_start = 0;
     bool timed_out = false;
+    unsigned backoff = KI_LOOKBACK_MIN_SLEEP_NS;
     while (true) {
-        const long long idx = end - (long long)lane;
-        uint64_t f;
-        unsigned pending;
+        uint64_t w[K];
+        int first_p, first_zero;  // lane-local positions (K = none)
+        int pos_p, pos_zero;      // window positions l*K+k of the first P / unpublished word
         while (true) {
-            f = (idx >= 0) ? load<Order::Acquire, Scope::Device>(&st.flags[idx]) : kFlagPrefix;
-            pending = __ballot_sync(0xffffffffu, f == kFlagNone);
-            if (!pending) break;
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const long long idx = end - (long long)(lane * K + k);
+                w[k] = (idx >= 0) ? load<Order::Relaxed, Scope::Device>(&st.words[idx]) : kFlagPrefix;
+            }
+            first_p = K;
+            first_zero = K;
+#pragma unroll
+            for (int k = K - 1; k >= 0; --k) {
+                if ((w[k] & 3) == kFlagPrefix) first_p = k;
+                if ((w[k] & 3) == kFlagNone) first_zero = k;
+            }
+            const unsigned pm = __ballot_sync(0xffffffffu, first_p < K);
+            const unsigned zm = __ballot_sync(0xffffffffu, first_zero < K);
+            const int lp = pm ? __ffs(pm) - 1 : 32, lz = zm ? __ffs(zm) - 1 : 32;
+            pos_p = (lp < 32) ? lp * K + __shfl_sync(0xffffffffu, first_p, lp) : 32 * K;
+            pos_zero = (lz < 32) ? lz * K + __shfl_sync(0xffffffffu, first_zero, lz) : 32 * K;
+            if (pos_zero > pos_p || (pos_zero == 32 * K && pos_p == 32 * K)) break;  // nothing missing before the P
             const uint64_t now = globaltimer_ns();
             if (t_start == 0) t_start = now;
             timed_out = __shfl_sync(0xffffffffu, (int)(now - t_start > timeout_ns), 0) != 0;
             if (timed_out) break;
-            __nanosleep(32);
+            __nanosleep(backoff);  // the window re-read is 32*K loads: back off to spare L2
+            if (backoff < KI_LOOKBACK_MAX_SLEEP_NS) backoff <<= 1;
         }
         if (timed_out) {
             if (lane == 0) atomicOr(status, (uint32_t)KI_DEV_TIMEOUT);
             break;
         }
+        // sum the words at positions <= pos_p (all of the window when it holds no P)
+        bool any_wide = false;
         int64_t v = 0;
-        if (idx >= 0) {
-            if (f == kFlagPrefix) v = load<Order::Relaxed, Scope::Device>(&st.incls[idx]);
-            else v = load<Order::Relaxed, Scope::Device>(&st.aggs[idx]);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int p = (int)lane * K + k;
+            if (p <= pos_p && p < 32 * K) {
+                if (w[k] & kFlagWide) any_wide = true;
+                else v = wrap_add(v, (int64_t)w[k] >> 3);
+            }
         }
-        const unsigned pmask = __ballot_sync(0xffffffffu, f == kFlagPrefix);
-        if (pmask) {
-            const unsigned first = (unsigned)(__ffs(pmask) - 1);
-            if (lane > first) v = 0;
-            excl = wrap_add(excl, warpfold(v, WrapAdd{}));
-            break;
+        if (__any_sync(0xffffffffu, any_wide)) {
+            fence<Scope::Device, Order::AcqRel>();
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int p = (int)lane * K + k;
+                const long long idx = end - p;
+                if (p <= pos_p && p < 32 * K && (w[k] & kFlagWide)) {
+                    const int64_t x = ((w[k] & 3) == kFlagPrefix) ? load<Order::Relaxed, Scope::Device>(&st.incls[idx])
+                                                                  : load<Order::Relaxed, Scope::Device>(&st.aggs[idx]);
+                    v = wrap_add(v, x);
+                }
+            }
         }
         excl = wrap_add(excl, warpfold(v, WrapAdd{}));
-        end -= 32;
+        if (pos_p < 32 * K) break;
+        end -= 32 * K;
     }
-    if (lane == 0) {
-        st.incls[t] = wrap_add(excl, agg);
-        store<Order::Release, Scope::Device>(&st.flags[t], kFlagPrefix);
-    }
+    if (lane == 0) publish(st, t, kFlagPrefix, wrap_add(excl, agg));
     return excl;
 }
 

@@ -1,16 +1,17 @@
 // scan.cu -- single-pass decoupled-lookback inclusive scan of Int64 (Base.cumsum semantics).
 //
-// One CTA per 4096-element tile (32 KiB), tiles handed out by an atomic ticket so that a tile's
-// predecessors are always owned by CTAs that already run (no deadlock on non-resident CTAs).
-// A full, 16-byte aligned tile is staged into shared memory with one 1-D TMA bulk copy
-// (cp.async.bulk ... mbarrier::complete_tx) and written back with one bulk store.
-//
-// Inside a tile, warp w owns elements [512w, 512w+512); lane l reads the pairs at 64j+2l (one
-// conflict-free 16-byte shared load per j).  Pass 1 folds each warp's 512 elements (xor fold,
-// @warpfold with every lane holding the total), warp 0 scans the 8 warp totals with @warpreduce,
-// publishes the tile aggregate and runs the decoupled lookback (ki/lookback.cuh) with
-// st.release.gpu / ld.acquire.gpu flags.  Pass 2 rescans each pair row with @warpreduce
-// (src/warp.jl:226-237) carrying the running prefix.
+// One CTA per 4096-element tile (256 threads).  The tile index comes from an atomic ticket taken
+// when the CTA starts, so a tile's predecessors are always owned by CTAs that already run, and a
+// tile's aggregate depends on nothing but its own data (no deadlock on non-resident CTAs, and no
+// CTA ever waits behind another CTA's unrelated work).  A full, 16-byte-aligned tile arrives in
+// shared memory by one 32 KiB 1-D TMA bulk copy (cp.async.bulk ... mbarrier::complete_tx).
+//   pass 1  warp w sums its 512 elements (8 rows of 32 lanes x 2 elements: conflict-free 16-byte
+//           shared loads), @warpfold (xor butterfly); warp 0 scans the 8 warp totals with
+//           @warpreduce, publishes the tile aggregate (ki/lookback.cuh: packed 64-bit status word,
+//           st.release.gpu) and looks back over a 256-tile window per L2 round trip;
+//   pass 2  each row is rescanned with @warpreduce (src/warp.jl:226-237) from the running prefix
+//           and stored straight to global memory with coalesced 16-byte streaming stores.
+// Tiles that are partial or not 16-byte aligned are staged with plain loads.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
@@ -23,6 +24,10 @@ constexpr int kTile = 4096;                 // elements per tile
 constexpr int kWarpSpan = kTile / kWarps;   // 512 elements per warp
 constexpr int kRows = kWarpSpan / 64;       // 8 rows of 32 lanes x 2 elements
 constexpr size_t kSmemBytes = kTile * sizeof(int64_t);
+#ifndef KI_SCAN_LOOKBACK_K
+#define KI_SCAN_LOOKBACK_K 1
+#endif
+constexpr int kLookbackK = KI_SCAN_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 
 struct ScanArgs {
     const int64_t* in;
@@ -33,12 +38,13 @@ struct ScanArgs {
     unsigned long long* ticket;
     uint32_t* status;
     uint64_t timeout_ns;
-    int use_tma;
+    int tma_in;   // input 16-byte aligned: full tiles come in by TMA
+    int vec_out;  // output 16-byte aligned: full tiles leave with 16-byte stores
 };
 
 __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    int64_t* tile = reinterpret_cast<int64_t*>(smem_raw);
+    int64_t* sb = reinterpret_cast<int64_t*>(smem_raw);
     __shared__ __align__(8) uint64_t bar;
     __shared__ int64_t warp_tot[kWarps];
     __shared__ int64_t warp_excl[kWarps];
@@ -48,7 +54,6 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
-
     if (tid == 0) {
         tile_id = atomicAdd(a.ticket, 1ull);
         ki::mbar_init(&bar, 1);
@@ -58,73 +63,68 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
     const uint64_t t = tile_id;
     const size_t first = (size_t)t * kTile;
     const int count = (int)min((size_t)kTile, a.n - first);
-    const bool bulk = a.use_tma && count == kTile;
-
+    const bool bulk = a.tma_in && count == kTile;
     if (bulk) {
         if (tid == 0) {
             ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
-            ki::bulk_g2s(tile, a.in + first, (uint32_t)kSmemBytes, &bar);
+            ki::bulk_g2s(sb, a.in + first, (uint32_t)kSmemBytes, &bar);
         }
-        if (!ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns)) {
-            // The copy is still in flight: wait for it once more (bounded) before touching smem.
-            ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns);
-        }
+        if (!ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns))
+            ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns);  // never leave a copy in flight
     } else {
-        for (int i = tid; i < kTile; i += kThreads) tile[i] = (i < count) ? a.in[first + i] : 0;
+        for (int i = tid; i < kTile; i += kThreads) sb[i] = (i < count) ? a.in[first + i] : 0;
         __syncthreads();
     }
+    const int wofs = w * kWarpSpan;
 
-    // ---- pass 1: per-warp totals --------------------------------------------------------------
-    const int64_t* wbase = tile + w * kWarpSpan;
+    // ---- pass 1: per-warp totals ----------------------------------------------------------------
     int64_t s = 0;
 #pragma unroll
     for (int j = 0; j < kRows; ++j) {
-        const longlong2 v = *reinterpret_cast<const longlong2*>(wbase + 64 * j + 2 * lane);
-        s = ki::wrap_add(s, ki::wrap_add(v.x, v.y));
+        const longlong2 p = *reinterpret_cast<const longlong2*>(sb + wofs + 64 * j + 2 * lane);
+        s = ki::wrap_add(s, ki::wrap_add(p.x, p.y));
     }
     s = ki::warpfold(s, ki::WrapAdd{});
     if (lane == 0) warp_tot[w] = s;
     __syncthreads();
 
-    // ---- tile aggregate, lookback ---------------------------------------------------------------
+    // ---- publish the aggregate, look back -------------------------------------------------------
     if (w == 0) {
-        const int64_t v = (lane < (unsigned)kWarps) ? warp_tot[lane] : 0;
-        const int64_t inc = ki::warpreduce(v, ki::WrapAdd{});
-        if (lane < (unsigned)kWarps) warp_excl[lane] = ki::wrap_sub(inc, v);
+        const int64_t x = (lane < (unsigned)kWarps) ? warp_tot[lane] : 0;
+        const int64_t inc = ki::warpreduce(x, ki::WrapAdd{});
+        if (lane < (unsigned)kWarps) warp_excl[lane] = ki::wrap_sub(inc, x);
         const int64_t agg = __shfl_sync(0xffffffffu, inc, kWarps - 1);
-        const int64_t ex = ki::decoupled_lookback(a.st, t, agg, a.seed, a.status, a.timeout_ns);
+        if (lane == 0) ki::publish_aggregate(a.st, t, agg, a.seed);
+        const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, t, agg, a.seed, a.status, a.timeout_ns);
         if (lane == 0) tile_excl = ex;
     }
     __syncthreads();
 
-    // ---- pass 2: scan rows with @warpreduce -----------------------------------------------------
+    // ---- pass 2: scan rows with @warpreduce, store ------------------------------------------------
     int64_t carry = ki::wrap_add(tile_excl, warp_excl[w]);
-    int64_t* wrow = tile + w * kWarpSpan;
+    const bool vec = a.vec_out && count == kTile;
 #pragma unroll
     for (int j = 0; j < kRows; ++j) {
-        longlong2* p = reinterpret_cast<longlong2*>(wrow + 64 * j + 2 * lane);
-        longlong2 v = *p;
-        const int64_t pair = ki::wrap_add(v.x, v.y);
+        const longlong2 p = *reinterpret_cast<const longlong2*>(sb + wofs + 64 * j + 2 * lane);
+        const int64_t pair = ki::wrap_add(p.x, p.y);
         const int64_t inc = ki::warpreduce(pair, ki::WrapAdd{});
-        const int64_t o0 = ki::wrap_add(ki::wrap_add(carry, ki::wrap_sub(inc, pair)), v.x);
-        v.y = ki::wrap_add(o0, v.y);
-        v.x = o0;
-        *p = v;
+        const int64_t o0 = ki::wrap_add(ki::wrap_add(carry, ki::wrap_sub(inc, pair)), p.x);
+        const int64_t o1 = ki::wrap_add(o0, p.y);
+        const int i = wofs + 64 * j + 2 * (int)lane;
+        if (vec) {
+            __stcs(reinterpret_cast<longlong2*>(a.out + first + i), make_longlong2(o0, o1));
+        } else {
+            if (i < count) a.out[first + i] = o0;
+            if (i + 1 < count) a.out[first + i + 1] = o1;
+        }
         carry = ki::wrap_add(carry, __shfl_sync(0xffffffffu, inc, 31));
     }
+}
 
-    if (bulk) {
-        ki::fence_proxy_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            ki::bulk_s2g(a.out + first, tile, (uint32_t)kSmemBytes);
-            ki::bulk_commit();
-            ki::bulk_wait_all();
-        }
-    } else {
-        __syncthreads();
-        for (int i = tid; i < count; i += kThreads) a.out[first + i] = tile[i];
-    }
+// Grid and launch shared by both entry points: one CTA per tile.
+void launch_scan(const ScanArgs& a, size_t ntiles, int sm_count, cudaStream_t s) {
+    (void)sm_count;
+    scan_i64_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
 }
 
 }  // namespace
@@ -144,15 +144,15 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     KI_GUARD(ctx);
     const size_t ntiles = (n + kTile - 1) / kTile;
     if (ntiles > (size_t)INT32_MAX) return ki::set_error(ctx, KI_ERR_ARG, "scan: n too large");
-    // scratch: [ticket (256 B)] [flags ntiles] [aggs ntiles] [incls ntiles]
-    const size_t flags_off = 256;
-    const size_t bytes = flags_off + ntiles * 24;
+    // scratch: [ticket (256 B)] [status words ntiles] [aggs ntiles] [incls ntiles]
+    const size_t words_off = 256;
+    const size_t bytes = words_off + ntiles * 24;
     void* base = nullptr;
     int rc = ki::ensure_region(ctx, KI_REG_SCAN, bytes, &base);
     if (rc) return rc;
     char* b = static_cast<char*>(base);
     cudaStream_t s = ki::as_stream(stream);
-    KI_CUDA(ctx, cudaMemsetAsync(b, 0, flags_off + ntiles * sizeof(uint64_t), s));
+    KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * sizeof(uint64_t), s));
 
     KI_CUDA(ctx, cudaFuncSetAttribute(scan_i64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kSmemBytes));
@@ -161,14 +161,15 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     a.out = d_out;
     a.n = n;
     a.seed = seed;
-    a.st.flags = reinterpret_cast<uint64_t*>(b + flags_off);
-    a.st.aggs = reinterpret_cast<int64_t*>(b + flags_off + ntiles * 8);
-    a.st.incls = reinterpret_cast<int64_t*>(b + flags_off + ntiles * 16);
+    a.st.words = reinterpret_cast<uint64_t*>(b + words_off);
+    a.st.aggs = reinterpret_cast<int64_t*>(b + words_off + ntiles * 8);
+    a.st.incls = reinterpret_cast<int64_t*>(b + words_off + ntiles * 16);
     a.ticket = reinterpret_cast<unsigned long long*>(b);
     a.status = ctx->d_status;
     a.timeout_ns = ctx->wait_timeout_ns;
-    a.use_tma = ki::aligned(d_in, 16) && ki::aligned(d_out, 16);
-    scan_i64_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
+    a.tma_in = ki::aligned(d_in, 16);
+    a.vec_out = ki::aligned(d_out, 16);
+    launch_scan(a, ntiles, ctx->sm_count, s);
     return ki::check_launch(ctx, "scan_i64_kernel launch");
 }
 
@@ -187,8 +188,8 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
 // is looked up once per device with cudaGetSymbolAddress (with that device current) and cached; the
 // first call on each device does this set-up and must therefore come before any stream capture.
 // All calls share the array and it keeps the last call's contents: each call clears the ticket, the
-// status word and the tile flags (cudaMemsetAsync on the cached address) before its launch, and
-// calls that overlap on the GPU (different streams, or several host threads) race on it.
+// status word and the tile status words (cudaMemsetAsync on the cached address) before its launch,
+// and calls that overlap on the GPU (different streams, or several host threads) race on it.
 // A bounded wait that runs out is latched in the array's status word and not reported; use the
 // context API where timeout reporting is needed.
 // ---------------------------------------------------------------------------------------------
@@ -201,6 +202,7 @@ static __device__ __align__(256) unsigned char g_scan_noalloc_scratch[kNoAllocHe
 struct NoAllocDevice {
     bool ready = false;
     unsigned char* scratch = nullptr;
+    int sm_count = 0;
 };
 std::mutex g_noalloc_mutex;
 NoAllocDevice g_noalloc_dev[64];
@@ -220,12 +222,15 @@ extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KI_ERR_CUDA;
     unsigned char* scratch = nullptr;
+    int sm_count = 0;
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mutex);
         NoAllocDevice& d = g_noalloc_dev[dev];
         if (!d.ready) {
             void* p = nullptr;
             if (cudaGetSymbolAddress(&p, g_scan_noalloc_scratch) != cudaSuccess || !p) return KI_ERR_CUDA;
+            if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+                return KI_ERR_CUDA;
             if (cudaFuncSetAttribute(scan_i64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kSmemBytes) != cudaSuccess)
                 return KI_ERR_CUDA;
@@ -233,6 +238,7 @@ extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out
             d.ready = true;
         }
         scratch = d.scratch;
+        sm_count = d.sm_count;
     }
     const size_t ntiles = (n + kTile - 1) / kTile;
     cudaStream_t s = ki::as_stream(stream);
@@ -243,13 +249,14 @@ extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out
     a.out = d_out;
     a.n = n;
     a.seed = seed;
-    a.st.flags = reinterpret_cast<uint64_t*>(scratch + kNoAllocHeader);
+    a.st.words = reinterpret_cast<uint64_t*>(scratch + kNoAllocHeader);
     a.st.aggs = reinterpret_cast<int64_t*>(scratch + kNoAllocHeader + kNoAllocTiles * 8);
     a.st.incls = reinterpret_cast<int64_t*>(scratch + kNoAllocHeader + kNoAllocTiles * 16);
     a.ticket = reinterpret_cast<unsigned long long*>(scratch);
     a.status = reinterpret_cast<uint32_t*>(scratch + 64);
     a.timeout_ns = 2000000000ull;
-    a.use_tma = ki::aligned(d_in, 16) && ki::aligned(d_out, 16);
-    scan_i64_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
+    a.tma_in = ki::aligned(d_in, 16);
+    a.vec_out = ki::aligned(d_out, 16);
+    launch_scan(a, ntiles, sm_count, s);
     return cudaGetLastError() == cudaSuccess ? KI_OK : KI_ERR_CUDA;
 }

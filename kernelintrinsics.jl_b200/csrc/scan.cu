@@ -1,16 +1,20 @@
 // scan.cu -- single-pass decoupled-lookback inclusive scan of Int64 (Base.cumsum semantics).
 //
-// One CTA per 4096-element tile (256 threads).  The tile index comes from an atomic ticket taken
-// when the CTA starts, so a tile's predecessors are always owned by CTAs that already run, and a
-// tile's aggregate depends on nothing but its own data (no deadlock on non-resident CTAs, and no
-// CTA ever waits behind another CTA's unrelated work).  A full, 16-byte-aligned tile arrives in
-// shared memory by one 32 KiB 1-D TMA bulk copy (cp.async.bulk ... mbarrier::complete_tx).
-//   pass 1  warp w sums its 512 elements (8 rows of 32 lanes x 2 elements: conflict-free 16-byte
-//           shared loads), @warpfold (xor butterfly); warp 0 scans the 8 warp totals with
-//           @warpreduce, publishes the tile aggregate (ki/lookback.cuh: packed 64-bit status word,
-//           st.release.gpu) and looks back over a 256-tile window per L2 round trip;
-//   pass 2  each row is rescanned with @warpreduce (src/warp.jl:226-237) from the running prefix
-//           and stored straight to global memory with coalesced 16-byte streaming stores.
+// Persistent CTAs, software-pipelined over tiles of 4096 elements, with 8 "work" warps and one
+// "look" warp.  Iteration k of a CTA runs two phases:
+//   phase A  work warps: wait for tile k (one 32 KiB 1-D TMA bulk copy, cp.async.bulk ...
+//            mbarrier::complete_tx), sum it (warp w folds its 512 elements with @warpfold over 8 rows
+//            of 32 lanes x 2 elements; warp 0 scans the 8 warp totals with @warpreduce) and publish
+//            its aggregate at once (ki/lookback.cuh: packed 64-bit status word, st.release.gpu);
+//            look warp, at the same time: the decoupled lookback of tile k-1;
+//   phase B  one thread takes the next ticket and starts its TMA into the (now free) tile buffer;
+//            work warps finish tile k-1: re-read its span from global memory (still in the 126 MB
+//            L2), rescan each row with @warpreduce (src/warp.jl:226-237) from the running prefix and
+//            store it with coalesced 16-byte streaming stores.
+// Between taking a ticket and publishing that tile's aggregate a CTA only waits for its own load and
+// its own second pass, never for a lookback, so no aggregate waits behind another tile; and the
+// ~1 us L2 round trips of a lookback overlap the next tile's load and first pass.  Tile indices
+// come from an atomic ticket, so a tile's predecessors are always taken by CTAs that already run.
 // Tiles that are partial or not 16-byte aligned are staged with plain loads.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
@@ -18,16 +22,22 @@
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kTile = 4096;                 // elements per tile
-constexpr int kWarpSpan = kTile / kWarps;   // 512 elements per warp
-constexpr int kRows = kWarpSpan / 64;       // 8 rows of 32 lanes x 2 elements
+constexpr int kWorkWarps = 8;
+constexpr int kLookWarp = kWorkWarps;
+constexpr int kWorkThreads = 32 * kWorkWarps;
+constexpr int kThreads = kWorkThreads + 32;
+constexpr int kTile = 4096;                     // elements per tile
+constexpr int kWarpSpan = kTile / kWorkWarps;   // 512 elements per work warp
+constexpr int kRows = kWarpSpan / 64;           // 8 rows of 32 lanes x 2 elements
 constexpr size_t kSmemBytes = kTile * sizeof(int64_t);
 #ifndef KI_SCAN_LOOKBACK_K
 #define KI_SCAN_LOOKBACK_K 1
 #endif
+#ifndef KI_SCAN_CTAS_PER_SM
+#define KI_SCAN_CTAS_PER_SM 3
+#endif
 constexpr int kLookbackK = KI_SCAN_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
+constexpr int kCtasPerSm = KI_SCAN_CTAS_PER_SM;
 
 struct ScanArgs {
     const int64_t* in;
@@ -42,89 +52,141 @@ struct ScanArgs {
     int vec_out;  // output 16-byte aligned: full tiles leave with 16-byte stores
 };
 
+struct Pending {
+    unsigned long long t;
+    int64_t agg;
+    int64_t tile_excl;
+    int64_t warp_excl[kWorkWarps];
+};
+
+__device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
+
 __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     int64_t* sb = reinterpret_cast<int64_t*>(smem_raw);
     __shared__ __align__(8) uint64_t bar;
-    __shared__ int64_t warp_tot[kWarps];
-    __shared__ int64_t warp_excl[kWarps];
-    __shared__ int64_t tile_excl;
-    __shared__ unsigned long long tile_id;
+    __shared__ int64_t warp_tot[kWorkWarps];
+    __shared__ Pending slot[2];  // tile k (being summed) and tile k-1 (being finished)
+    __shared__ unsigned long long ticket;
 
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
+    const uint64_t ntiles = (a.n + kTile - 1) / kTile;
+    auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
+    auto fetch = [&]() {  // take a ticket and start its load (thread 0)
+        const unsigned long long t = atomicAdd(a.ticket, 1ull);
+        ticket = t;
+        if (bulk_ok(t)) {
+            ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
+            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
+            ki::bulk_g2s(sb, a.in + t * kTile, (uint32_t)kSmemBytes, &bar);
+        }
+    };
     if (tid == 0) {
-        tile_id = atomicAdd(a.ticket, 1ull);
         ki::mbar_init(&bar, 1);
         ki::fence_mbar_init();
+        fetch();
     }
     __syncthreads();
-    const uint64_t t = tile_id;
-    const size_t first = (size_t)t * kTile;
-    const int count = (int)min((size_t)kTile, a.n - first);
-    const bool bulk = a.tma_in && count == kTile;
-    if (bulk) {
-        if (tid == 0) {
-            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
-            ki::bulk_g2s(sb, a.in + first, (uint32_t)kSmemBytes, &bar);
-        }
-        if (!ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns))
-            ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns);  // never leave a copy in flight
-    } else {
-        for (int i = tid; i < kTile; i += kThreads) sb[i] = (i < count) ? a.in[first + i] : 0;
-        __syncthreads();
-    }
-    const int wofs = w * kWarpSpan;
 
-    // ---- pass 1: per-warp totals ----------------------------------------------------------------
-    int64_t s = 0;
+    uint32_t phase = 0;
+    bool have_old = false;
+    int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
+    while (true) {
+        const uint64_t t_new = ticket;
+        const bool new_valid = t_new < ntiles;
+        if (!new_valid && !have_old) break;
+
+        // ---- phase A: sum and publish tile k  ||  look back for tile k-1 ---------------------------
+        if (w == kLookWarp) {
+            if (have_old) {
+                Pending& o = slot[cur ^ 1];
+                const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, a.seed, a.status,
+                                                                      a.timeout_ns);
+                if (lane == 0) o.tile_excl = ex;
+            }
+        } else if (new_valid) {
+            const size_t first = (size_t)t_new * kTile;
+            const int count = (int)min((size_t)kTile, a.n - first);
+            if (bulk_ok(t_new)) {
+                if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
+                    ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
+                phase ^= 1u;
+            } else {
+                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.in[first + i] : 0;
+                work_sync();
+            }
+            int64_t s = 0;
 #pragma unroll
-    for (int j = 0; j < kRows; ++j) {
-        const longlong2 p = *reinterpret_cast<const longlong2*>(sb + wofs + 64 * j + 2 * lane);
-        s = ki::wrap_add(s, ki::wrap_add(p.x, p.y));
-    }
-    s = ki::warpfold(s, ki::WrapAdd{});
-    if (lane == 0) warp_tot[w] = s;
-    __syncthreads();
-
-    // ---- publish the aggregate, look back -------------------------------------------------------
-    if (w == 0) {
-        const int64_t x = (lane < (unsigned)kWarps) ? warp_tot[lane] : 0;
-        const int64_t inc = ki::warpreduce(x, ki::WrapAdd{});
-        if (lane < (unsigned)kWarps) warp_excl[lane] = ki::wrap_sub(inc, x);
-        const int64_t agg = __shfl_sync(0xffffffffu, inc, kWarps - 1);
-        if (lane == 0) ki::publish_aggregate(a.st, t, agg, a.seed);
-        const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, t, agg, a.seed, a.status, a.timeout_ns);
-        if (lane == 0) tile_excl = ex;
-    }
-    __syncthreads();
-
-    // ---- pass 2: scan rows with @warpreduce, store ------------------------------------------------
-    int64_t carry = ki::wrap_add(tile_excl, warp_excl[w]);
-    const bool vec = a.vec_out && count == kTile;
-#pragma unroll
-    for (int j = 0; j < kRows; ++j) {
-        const longlong2 p = *reinterpret_cast<const longlong2*>(sb + wofs + 64 * j + 2 * lane);
-        const int64_t pair = ki::wrap_add(p.x, p.y);
-        const int64_t inc = ki::warpreduce(pair, ki::WrapAdd{});
-        const int64_t o0 = ki::wrap_add(ki::wrap_add(carry, ki::wrap_sub(inc, pair)), p.x);
-        const int64_t o1 = ki::wrap_add(o0, p.y);
-        const int i = wofs + 64 * j + 2 * (int)lane;
-        if (vec) {
-            __stcs(reinterpret_cast<longlong2*>(a.out + first + i), make_longlong2(o0, o1));
-        } else {
-            if (i < count) a.out[first + i] = o0;
-            if (i + 1 < count) a.out[first + i + 1] = o1;
+            for (int j = 0; j < kRows; ++j) {
+                const longlong2 p = *reinterpret_cast<const longlong2*>(sb + w * kWarpSpan + 64 * j + 2 * lane);
+                s = ki::wrap_add(s, ki::wrap_add(p.x, p.y));
+            }
+            s = ki::warpfold(s, ki::WrapAdd{});
+            if (lane == 0) warp_tot[w] = s;
+            work_sync();
+            if (w == 0) {
+                const int64_t x = (lane < (unsigned)kWorkWarps) ? warp_tot[lane] : 0;
+                const int64_t inc = ki::warpreduce(x, ki::WrapAdd{});
+                const int64_t agg = __shfl_sync(0xffffffffu, inc, kWorkWarps - 1);
+                Pending& e = slot[cur];
+                if (lane < (unsigned)kWorkWarps) e.warp_excl[lane] = ki::wrap_sub(inc, x);
+                if (lane == 0) {
+                    e.t = t_new;
+                    e.agg = agg;
+                    ki::publish_aggregate(a.st, t_new, agg, a.seed);
+                }
+            }
         }
-        carry = ki::wrap_add(carry, __shfl_sync(0xffffffffu, inc, 31));
+        __syncthreads();  // tile k summed (buffer free, slot written); tile k-1's prefix known
+
+        // ---- phase B: start tile k+1's load; finish tile k-1 ------------------------------------------
+        if (tid == 0 && new_valid) fetch();
+        if (w < kWorkWarps && have_old) {
+            const Pending& o = slot[cur ^ 1];
+            const size_t first = (size_t)o.t * kTile;
+            const int count = (int)min((size_t)kTile, a.n - first);
+            const bool full = count == kTile;
+            int64_t carry = ki::wrap_add(o.tile_excl, o.warp_excl[w]);
+            longlong2 v[kRows];
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {  // all loads in flight before the scan
+                const int i = w * kWarpSpan + 64 * j + 2 * (int)lane;
+                if (full && a.tma_in) {
+                    v[j] = *reinterpret_cast<const longlong2*>(a.in + first + i);
+                } else {
+                    v[j].x = (i < count) ? a.in[first + i] : 0;
+                    v[j].y = (i + 1 < count) ? a.in[first + i + 1] : 0;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {
+                const int64_t pair = ki::wrap_add(v[j].x, v[j].y);
+                const int64_t inc = ki::warpreduce(pair, ki::WrapAdd{});
+                const int64_t o0 = ki::wrap_add(ki::wrap_add(carry, ki::wrap_sub(inc, pair)), v[j].x);
+                const int64_t o1 = ki::wrap_add(o0, v[j].y);
+                const int i = w * kWarpSpan + 64 * j + 2 * (int)lane;
+                if (full && a.vec_out) {
+                    __stcs(reinterpret_cast<longlong2*>(a.out + first + i), make_longlong2(o0, o1));
+                } else {
+                    if (i < count) a.out[first + i] = o0;
+                    if (i + 1 < count) a.out[first + i + 1] = o1;
+                }
+                carry = ki::wrap_add(carry, __shfl_sync(0xffffffffu, inc, 31));
+            }
+        }
+        __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
+        have_old = new_valid;
+        cur ^= 1;
     }
 }
 
-// Grid and launch shared by both entry points: one CTA per tile.
+// Grid and launch shared by both entry points: persistent, kCtasPerSm CTAs per SM.
 void launch_scan(const ScanArgs& a, size_t ntiles, int sm_count, cudaStream_t s) {
-    (void)sm_count;
-    scan_i64_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
+    size_t grid = (size_t)sm_count * kCtasPerSm;
+    if (grid > ntiles) grid = ntiles;
+    scan_i64_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(a);
 }
 
 }  // namespace

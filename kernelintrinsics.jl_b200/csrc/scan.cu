@@ -7,7 +7,7 @@
 //            of 32 lanes x 2 elements; warp 0 scans the 8 warp totals with @warpreduce) and publish
 //            its aggregate at once (ki/lookback.cuh: packed 64-bit status word, st.release.gpu);
 //            look warp, at the same time: the decoupled lookback of tile k-1;
-//   phase B  one thread takes the next ticket and starts its TMA into the (now free) tile buffer;
+//   phase B  the look warp takes the next ticket and starts its TMA into the (now free) tile buffer;
 //            work warps finish tile k-1: re-read its span from global memory (still in the 126 MB
 //            L2), rescan each row with @warpreduce (src/warp.jl:226-237) from the running prefix and
 //            store it with coalesced 16-byte streaming stores.
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
     const unsigned lane = tid & 31;
     const uint64_t ntiles = (a.n + kTile - 1) / kTile;
     auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
-    auto fetch = [&]() {  // take a ticket and start its load (thread 0)
+    auto fetch = [&]() {  // take a ticket and start its load (one thread)
         const unsigned long long t = atomicAdd(a.ticket, 1ull);
         ticket = t;
         if (bulk_ok(t)) {
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
         __syncthreads();  // tile k summed (buffer free, slot written); tile k-1's prefix known
 
         // ---- phase B: start tile k+1's load; finish tile k-1 ------------------------------------------
-        if (tid == 0 && new_valid) fetch();
+        if (tid == kLookWarp * 32 && new_valid) fetch();  // the look warp is idle in phase B
         if (w < kWorkWarps && have_old) {
             const Pending& o = slot[cur ^ 1];
             const size_t first = (size_t)o.t * kTile;

@@ -1,36 +1,49 @@
 // compact.cu -- order-preserving stream compaction: filter(x -> x > t, x) and findall.
 //
-// One CTA per 4096-element tile (256 threads); the tile index comes from an atomic ticket taken
-// when the CTA starts (predecessors always run; a tile's count depends only on its own data).
-// A full, 16-byte-aligned tile arrives in shared memory by one 16 KiB 1-D TMA bulk copy.  Warp w
-// owns elements [512w, 512w+512) as 4 rows; in row j lane l holds the float4 at 128j + 4l
-// (conflict-free 16-byte shared loads).  For each of the 4 components the warp takes a @vote Ballot
-// (ext/CUDA/shuffle_vote.jl:23-34, vote.sync ballot -> UInt32), and an element's rank inside its row
-// is
-//     sum over components c of popc(ballot_c & lanes_below) + (kept components before it in its lane)
-// which keeps source order (lane-major, then component).  Warp counts are scanned by warp 0 with
-// @warpreduce, the tile count is published at once and goes through the decoupled lookback
-// (ki/lookback.cuh), and the kept values and their indices are packed in shared memory, shifted by
-// the output's alignment residue so that the copy-out uses coalesced 16-byte stores into
-// [tile prefix, tile prefix + tile count).
+// Persistent CTAs (3 per SM), software-pipelined over tiles of 16384 elements, with 8 "work" warps
+// and one "look" warp, the same pipeline as scan.cu.  Iteration k of a CTA runs two phases:
+//   phase A  work warps: wait for tile k (one 64 KiB 1-D TMA bulk copy, cp.async.bulk ...
+//            mbarrier::complete_tx) and count its kept elements (warp w owns 2048 elements as 16 rows
+//            of 32 lanes x float4: conflict-free 16-byte shared loads); warp 0 scans the 8 warp
+//            counts with @warpreduce and publishes the tile count at once (ki/lookback.cuh);
+//            look warp, at the same time: the decoupled lookback of tile k-1;
+//   phase B  the look warp takes the next ticket and starts its TMA into the free buffer;
+//            work warps write tile k-1: re-read it from global memory (still in the 126 MB L2) and,
+//            for each row and component c, take a @vote Ballot (ext/CUDA/shuffle_vote.jl:23-34,
+//            vote.sync ballot -> UInt32).  An element's rank inside its row is
+//                sum over c of popc(ballot_c & lanes_below) + (kept components before it in its lane)
+//            which keeps source order (lane-major, then component); kept values and their indices
+//            are stored at tile prefix + warp prefix + row prefix + rank.
+// Between taking a ticket and publishing that tile's count a CTA only waits for its own load and
+// its own second pass, never for a lookback.  Tiles that are partial or not 16-byte aligned are read
+// with plain loads.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kTile = 4096;
-constexpr int kWarpSpan = kTile / kWarps;  // 512
-constexpr int kRows = kWarpSpan / 128;     // 4 rows of 32 lanes x float4
-constexpr size_t kBufBytes = kTile * sizeof(float);              // 16 KiB
-constexpr size_t kStageElems = kTile + 4;                        // room for the alignment shift
-constexpr size_t kSmemBytes = kBufBytes + kStageElems * 8;
 #ifndef KI_COMPACT_LOOKBACK_K
 #define KI_COMPACT_LOOKBACK_K 1
 #endif
+#ifndef KI_COMPACT_TILE
+#define KI_COMPACT_TILE 16384
+#endif
+#ifndef KI_COMPACT_CTAS_PER_SM
+#define KI_COMPACT_CTAS_PER_SM 3
+#endif
+constexpr int kWorkWarps = 8;
+constexpr int kLookWarp = kWorkWarps;
+constexpr int kWorkThreads = 32 * kWorkWarps;
+constexpr int kThreads = kWorkThreads + 32;
+constexpr int kTile = KI_COMPACT_TILE;
+constexpr int kWarpSpan = kTile / kWorkWarps;   // elements per work warp
+constexpr int kRows = kWarpSpan / 128;          // rows of 32 lanes x float4
+static_assert(kWarpSpan % 128 == 0, "tile must split into rows of 128 elements per warp");
+constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
+constexpr size_t kSmemBytes = kTile * sizeof(float);
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
+constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 
 struct CompactArgs {
     const float* x;
@@ -44,144 +57,152 @@ struct CompactArgs {
     unsigned long long* ticket;
     uint32_t* status;
     uint64_t timeout_ns;
-    int tma_in;   // x is 16-byte aligned
-    int vec_out;  // out_vals and out_idx are 16-byte aligned (or absent)
+    int tma_in;  // x is 16-byte aligned: full tiles come in by TMA, rows by float4
 };
+
+struct Pending {
+    unsigned long long t;
+    int64_t agg;
+    int64_t tile_excl;
+    int warp_excl[kWorkWarps];
+};
+
+__device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
 
 __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ int warp_cnt[kWarps];
-    __shared__ int warp_excl[kWarps];
-    __shared__ int tile_cnt;
-    __shared__ int64_t tile_excl;
-    __shared__ unsigned long long tile_id;
-
     float* sb = reinterpret_cast<float*>(smem_raw);
-    float* stage_v = reinterpret_cast<float*>(smem_raw + kBufBytes);
-    int32_t* stage_i = reinterpret_cast<int32_t*>(smem_raw + kBufBytes + kStageElems * 4);
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int warp_cnt[kWorkWarps];
+    __shared__ Pending slot[2];  // tile k (being counted) and tile k-1 (being written)
+    __shared__ unsigned long long ticket;
+
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
     const uint64_t ntiles = (a.n + kTile - 1) / kTile;
+    auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
+    auto fetch = [&]() {  // take a ticket and start its load (one thread)
+        const unsigned long long t = atomicAdd(a.ticket, 1ull);
+        ticket = t;
+        if (bulk_ok(t)) {
+            ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
+            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
+            ki::bulk_g2s(sb, a.x + t * kTile, (uint32_t)kSmemBytes, &bar);
+        }
+    };
     if (tid == 0) {
-        tile_id = atomicAdd(a.ticket, 1ull);
         ki::mbar_init(&bar, 1);
         ki::fence_mbar_init();
+        fetch();
     }
     __syncthreads();
-    const uint64_t t = tile_id;
-    const size_t first = (size_t)t * kTile;
-    const int count = (int)min((size_t)kTile, a.n - first);
-    const int wofs = w * kWarpSpan;
-    if (a.tma_in && count == kTile) {
-        if (tid == 0) {
-            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kBufBytes);
-            ki::bulk_g2s(sb, a.x + first, (uint32_t)kBufBytes, &bar);
-        }
-        if (!ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns))
-            ki::mbar_wait_bounded(&bar, 0, a.status, a.timeout_ns);  // never leave a copy in flight
-    } else {
-        for (int i = tid; i < kTile; i += kThreads) sb[i] = (i < count) ? a.x[first + i] : 0.0f;
-        __syncthreads();
-    }
 
-    // predicates (elements past the end never pass) and ballots
     const unsigned below = (1u << lane) - 1u;  // lanes with a lower index
-    float4 v[kRows];
-    unsigned pbits = 0;  // bit 4j+c
-#pragma unroll
-    for (int j = 0; j < kRows; ++j) {
-        v[j] = reinterpret_cast<const float4*>(sb + wofs)[32 * j + lane];
-        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int i = wofs + 128 * j + 4 * (int)lane + c;
-            if (i < count && e[c] > a.thr) pbits |= 1u << (4 * j + c);
-        }
-    }
-    int rank0[kRows];  // kept elements of the row before this lane
-    int row_cnt[kRows];
-    int wcount = 0;
-#pragma unroll
-    for (int j = 0; j < kRows; ++j) {
-        rank0[j] = 0;
-        row_cnt[j] = 0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const unsigned bal = ki::ballot((pbits >> (4 * j + c)) & 1u);
-            rank0[j] += __popc(bal & below);
-            row_cnt[j] += __popc(bal);
-        }
-        wcount += row_cnt[j];
-    }
-    if (lane == 0) warp_cnt[w] = wcount;
-    __syncthreads();
+    uint32_t phase = 0;
+    bool have_old = false;
+    int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
+    while (true) {
+        const uint64_t t_new = ticket;
+        const bool new_valid = t_new < ntiles;
+        if (!new_valid && !have_old) break;
 
-    if (w == 0) {
-        const int c = (lane < (unsigned)kWarps) ? warp_cnt[lane] : 0;
-        const int inc = ki::warpreduce(c, ki::Add{});
-        if (lane < (unsigned)kWarps) warp_excl[lane] = inc - c;
-        const int agg = __shfl_sync(0xffffffffu, inc, kWarps - 1);
-        if (lane == 0) ki::publish_aggregate(a.st, t, agg, 0);
-        const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, t, agg, 0, a.status, a.timeout_ns);
-        if (lane == 0) {
-            tile_excl = ex;
-            tile_cnt = agg;
-            if (t == ntiles - 1 && a.d_count) *a.d_count = (uint64_t)(ex + agg);
-        }
-    }
-    __syncthreads();
-
-    // pack the kept elements in source order, shifted by the output alignment residue
-    const int64_t tex = tile_excl;
-    const int shift = (int)(tex & 3);
-    int pos = warp_excl[w] + shift;
-#pragma unroll
-    for (int j = 0; j < kRows; ++j) {
-        int r = pos + rank0[j];
-        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            if ((pbits >> (4 * j + c)) & 1u) {
-                stage_v[r] = e[c];
-                stage_i[r] = (int32_t)((int64_t)(first + wofs + 128 * j + 4 * lane + c) + a.index_base);
-                ++r;
+        // ---- phase A: count and publish tile k  ||  look back for tile k-1 -------------------------
+        if (w == kLookWarp) {
+            if (have_old) {
+                Pending& o = slot[cur ^ 1];
+                const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, 0, a.status, a.timeout_ns);
+                if (lane == 0) o.tile_excl = ex;
+            }
+        } else if (new_valid) {
+            const size_t first = (size_t)t_new * kTile;
+            const int count = (int)min((size_t)kTile, a.n - first);
+            if (bulk_ok(t_new)) {
+                if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
+                    ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
+                phase ^= 1u;
+            } else {
+                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.x[first + i] : 0.0f;
+                work_sync();
+            }
+            int c = 0;
+#pragma unroll 4
+            for (int j = 0; j < kRows; ++j) {
+                const int i0 = w * kWarpSpan + 128 * j + 4 * (int)lane;
+                const float4 v = *reinterpret_cast<const float4*>(sb + i0);
+                c += (i0 + 0 < count && v.x > a.thr) + (i0 + 1 < count && v.y > a.thr) +
+                     (i0 + 2 < count && v.z > a.thr) + (i0 + 3 < count && v.w > a.thr);
+            }
+            c = ki::warpfold(c, ki::Add{});
+            if (lane == 0) warp_cnt[w] = c;
+            work_sync();
+            if (w == 0) {
+                const int x = (lane < (unsigned)kWorkWarps) ? warp_cnt[lane] : 0;
+                const int inc = ki::warpreduce(x, ki::Add{});
+                const int agg = __shfl_sync(0xffffffffu, inc, kWorkWarps - 1);
+                Pending& e = slot[cur];
+                if (lane < (unsigned)kWorkWarps) e.warp_excl[lane] = inc - x;
+                if (lane == 0) {
+                    e.t = t_new;
+                    e.agg = agg;
+                    ki::publish_aggregate(a.st, t_new, agg, 0);
+                }
             }
         }
-        pos += row_cnt[j];
-    }
-    __syncthreads();
+        __syncthreads();  // tile k counted (buffer free, slot written); tile k-1's prefix known
 
-    // copy out [tex, tex + cnt): staged element k sits at stage[k + shift]
-    const int cnt = tile_cnt;
-    if (a.vec_out) {
-        const int to_boundary = (4 - shift) & 3;  // elements before the first 16-byte boundary
-        const int head = to_boundary < cnt ? to_boundary : cnt;
-        if (tid < head) {
-            if (a.out_vals) a.out_vals[tex + tid] = stage_v[shift + tid];
-            if (a.out_idx) a.out_idx[tex + tid] = stage_i[shift + tid];
+        // ---- phase B: start tile k+1's load; write tile k-1 -------------------------------------------
+        if (tid == kLookWarp * 32 && new_valid) fetch();  // the look warp is idle in phase B
+        if (w < kWorkWarps && have_old) {
+            const Pending& o = slot[cur ^ 1];
+            const size_t first = (size_t)o.t * kTile;
+            const int count = (int)min((size_t)kTile, a.n - first);
+            const bool vec_in = a.tma_in && count == kTile;
+            int64_t pos = o.tile_excl + o.warp_excl[w];
+            for (int j0 = 0; j0 < kRows; j0 += kBatch) {
+                float4 v[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {  // all loads in flight first
+                    const int i0 = w * kWarpSpan + 128 * (j0 + j) + 4 * (int)lane;
+                    if (vec_in) {
+                        v[j] = *reinterpret_cast<const float4*>(a.x + first + i0);
+                    } else {
+                        v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : 0.0f;
+                        v[j].y = (i0 + 1 < count) ? a.x[first + i0 + 1] : 0.0f;
+                        v[j].z = (i0 + 2 < count) ? a.x[first + i0 + 2] : 0.0f;
+                        v[j].w = (i0 + 3 < count) ? a.x[first + i0 + 3] : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int i0 = w * kWarpSpan + 128 * (j0 + j) + 4 * (int)lane;
+                    const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                    bool p[4];
+                    int rank = 0, row = 0;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        p[q] = (i0 + q < count) && e[q] > a.thr;
+                        const unsigned bal = ki::ballot(p[q]);
+                        rank += __popc(bal & below);
+                        row += __popc(bal);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (p[q]) {
+                            const int64_t o_at = pos + rank;
+                            if (a.out_vals) a.out_vals[o_at] = e[q];
+                            if (a.out_idx) a.out_idx[o_at] = (int32_t)((int64_t)(first + i0 + q) + a.index_base);
+                            ++rank;
+                        }
+                    }
+                    pos += row;
+                }
+            }
+            if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);
         }
-        const int nvec = (cnt - head) >> 2;
-        const int s0 = shift + head;  // multiple of 4
-        for (int q = tid; q < nvec; q += kThreads) {
-            if (a.out_vals)
-                __stcs(reinterpret_cast<float4*>(a.out_vals + tex + head) + q,
-                       reinterpret_cast<const float4*>(stage_v + s0)[q]);
-            if (a.out_idx)
-                __stcs(reinterpret_cast<int4*>(a.out_idx + tex + head) + q,
-                       reinterpret_cast<const int4*>(stage_i + s0)[q]);
-        }
-        const int t0 = head + 4 * nvec;
-        if (tid < cnt - t0) {
-            if (a.out_vals) a.out_vals[tex + t0 + tid] = stage_v[shift + t0 + tid];
-            if (a.out_idx) a.out_idx[tex + t0 + tid] = stage_i[shift + t0 + tid];
-        }
-    } else {
-        for (int k = tid; k < cnt; k += kThreads) {
-            if (a.out_vals) a.out_vals[tex + k] = stage_v[shift + k];
-            if (a.out_idx) a.out_idx[tex + k] = stage_i[shift + k];
-        }
+        __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
+        have_old = new_valid;
+        cur ^= 1;
     }
 }
 
@@ -226,7 +247,8 @@ extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float 
     a.status = ctx->d_status;
     a.timeout_ns = ctx->wait_timeout_ns;
     a.tma_in = ki::aligned(d_x, 16);
-    a.vec_out = (!d_out_vals || ki::aligned(d_out_vals, 16)) && (!d_out_idx || ki::aligned(d_out_idx, 16));
-    compact_gt_f32_kernel<<<(unsigned)ntiles, kThreads, kSmemBytes, s>>>(a);
+    size_t grid = (size_t)ctx->sm_count * kCtasPerSm;
+    if (grid > ntiles) grid = ntiles;
+    compact_gt_f32_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(a);
     return ki::check_launch(ctx, "compact_gt_f32_kernel launch");
 }

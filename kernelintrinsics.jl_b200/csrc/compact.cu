@@ -21,6 +21,18 @@
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
 
+// Tiles are read twice: once by TMA for the first pass, once from L2 for the second.
+#ifndef KI_KEEP_TILES
+#define KI_KEEP_TILES 1
+#endif
+#if KI_KEEP_TILES
+#define KI_G2S ki::bulk_g2s_keep
+#define KI_RELOAD(p) __ldcs(p)
+#else
+#define KI_G2S ki::bulk_g2s
+#define KI_RELOAD(p) (*(p))
+#endif
+
 namespace {
 
 #ifndef KI_COMPACT_LOOKBACK_K
@@ -88,7 +100,7 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         if (bulk_ok(t)) {
             ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
             ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
-            ki::bulk_g2s(sb, a.x + t * kTile, (uint32_t)kSmemBytes, &bar);
+            KI_G2S(sb, a.x + t * kTile, (uint32_t)kSmemBytes, &bar);
         }
     };
     if (tid == 0) {
@@ -165,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
                 for (int j = 0; j < kBatch; ++j) {  // all loads in flight first
                     const int i0 = w * kWarpSpan + 128 * (j0 + j) + 4 * (int)lane;
                     if (vec_in) {
-                        v[j] = *reinterpret_cast<const float4*>(a.x + first + i0);
+                        v[j] = KI_RELOAD(reinterpret_cast<const float4*>(a.x + first + i0));
                     } else {
                         v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : 0.0f;
                         v[j].y = (i0 + 1 < count) ? a.x[first + i0 + 1] : 0.0f;

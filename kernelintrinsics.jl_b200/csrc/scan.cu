@@ -20,6 +20,18 @@
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
 
+// Tiles are read twice: once by TMA for the first pass, once from L2 for the second.
+#ifndef KI_KEEP_TILES
+#define KI_KEEP_TILES 1
+#endif
+#if KI_KEEP_TILES
+#define KI_G2S ki::bulk_g2s_keep
+#define KI_RELOAD(p) __ldcs(p)
+#else
+#define KI_G2S ki::bulk_g2s
+#define KI_RELOAD(p) (*(p))
+#endif
+
 namespace {
 
 constexpr int kWorkWarps = 8;
@@ -80,7 +92,7 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
         if (bulk_ok(t)) {
             ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
             ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
-            ki::bulk_g2s(sb, a.in + t * kTile, (uint32_t)kSmemBytes, &bar);
+            KI_G2S(sb, a.in + t * kTile, (uint32_t)kSmemBytes, &bar);
         }
     };
     if (tid == 0) {
@@ -154,7 +166,7 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
             for (int j = 0; j < kRows; ++j) {  // all loads in flight before the scan
                 const int i = w * kWarpSpan + 64 * j + 2 * (int)lane;
                 if (full && a.tma_in) {
-                    v[j] = *reinterpret_cast<const longlong2*>(a.in + first + i);
+                    v[j] = KI_RELOAD(reinterpret_cast<const longlong2*>(a.in + first + i));
                 } else {
                     v[j].x = (i < count) ? a.in[first + i] : 0;
                     v[j].y = (i + 1 < count) ? a.in[first + i + 1] : 0;

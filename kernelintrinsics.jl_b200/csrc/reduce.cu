@@ -14,10 +14,19 @@
 
 namespace {
 
-constexpr int kThreads = 256;
+#ifndef KI_REDUCE_THREADS
+#define KI_REDUCE_THREADS 256
+#endif
+#ifndef KI_REDUCE_UNROLL
+#define KI_REDUCE_UNROLL 4
+#endif
+#ifndef KI_REDUCE_BLOCKS_PER_SM
+#define KI_REDUCE_BLOCKS_PER_SM 8
+#endif
+constexpr int kThreads = KI_REDUCE_THREADS;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 4;
-constexpr int kBlocksPerSm = 8;
+constexpr int kUnroll = KI_REDUCE_UNROLL;          // 16-byte loads in flight per thread
+constexpr int kBlocksPerSm = KI_REDUCE_BLOCKS_PER_SM;
 
 template <class T>
 struct Acc;

@@ -16,10 +16,22 @@
 
 namespace {
 
-constexpr int kThreads = 512;
-constexpr int kUnroll = 4;               // 32-chunk rows per warp span
+#ifndef KI_COPY_THREADS
+#define KI_COPY_THREADS 512
+#endif
+#ifndef KI_COPY_UNROLL
+#define KI_COPY_UNROLL 4
+#endif
+#ifndef KI_COPY_BLOCKS_PER_SM
+#define KI_COPY_BLOCKS_PER_SM 4
+#endif
+#ifndef KI_COPY_MIN_BLOCKS
+#define KI_COPY_MIN_BLOCKS 1
+#endif
+constexpr int kThreads = KI_COPY_THREADS;
+constexpr int kUnroll = KI_COPY_UNROLL;  // 32-chunk rows per warp span
 constexpr int kSpan = 32 * kUnroll;      // 16-byte chunks per warp span
-constexpr int kBlocksPerSm = 4;
+constexpr int kBlocksPerSm = KI_COPY_BLOCKS_PER_SM;
 
 template <int WS>
 __device__ __forceinline__ uint4 realign(const uint4& lo, const uint4& hi, unsigned sh) {
@@ -53,7 +65,7 @@ struct CopyArgs {
 
 // WS = source misalignment / 4 within a 16-byte word; ALIGNED when the misalignment is 0.
 template <int WS, bool ALIGNED>
-__global__ void __launch_bounds__(kThreads) vcopy_kernel(CopyArgs a) {
+__global__ void __launch_bounds__(kThreads, KI_COPY_MIN_BLOCKS) vcopy_kernel(CopyArgs a) {
     const unsigned lane = threadIdx.x & 31;
     uint4* __restrict__ d = reinterpret_cast<uint4*>(a.dst + a.head);
     const uint4* __restrict__ sa = a.src_al;

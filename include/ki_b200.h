@@ -93,6 +93,13 @@ int ki_ctx_set_wait_timeout_ns(ki_ctx* ctx, uint64_t ns);
  * Semantics of copyto!(dst, src) on nbytes bytes; any byte alignment of dst and src.
  * dst and src must not overlap (KI_ERR_ARG). */
 int ki_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream);
+/* copyto! between two HOST buffers through the device: the bytes cross to the device in chunks,
+ * are copied there by the same kernel as ki_vcopy and come back, with both copy directions and the
+ * kernel overlapped (chunks cycle over device staging slots owned by the context).  Asynchronous
+ * with respect to the host when both buffers are page-locked (cudaHostAlloc / cudaHostRegister);
+ * the copy is complete when `stream` is.  dst and src must not overlap (KI_ERR_ARG).  Not
+ * re-entrant on one context: two calls in flight on different streams share the staging slots. */
+int ki_vcopy_host(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream);
 
 /* ---- (a3) grid-wide reduce (@warpfold, src/warp.jl:273-282) ---------------------------------
  * sum(x) of n Float32 values, accumulated in Float64 across threads; writes the Float32 result to

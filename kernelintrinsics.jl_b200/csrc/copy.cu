@@ -22,16 +22,18 @@ namespace {
 #ifndef KI_COPY_UNROLL
 #define KI_COPY_UNROLL 4
 #endif
-#ifndef KI_COPY_BLOCKS_PER_SM
-#define KI_COPY_BLOCKS_PER_SM 4
-#endif
 #ifndef KI_COPY_MIN_BLOCKS
 #define KI_COPY_MIN_BLOCKS 1
+#endif
+#ifndef KI_COPY_WAVES
+#define KI_COPY_WAVES 2  // grid = whole waves of resident blocks
+#endif
+#ifndef KI_PIPE_CHUNK
+#define KI_PIPE_CHUNK (16u << 20)  // host-buffer copy: bytes per pipelined chunk
 #endif
 constexpr int kThreads = KI_COPY_THREADS;
 constexpr int kUnroll = KI_COPY_UNROLL;  // 32-chunk rows per warp span
 constexpr int kSpan = 32 * kUnroll;      // 16-byte chunks per warp span
-constexpr int kBlocksPerSm = KI_COPY_BLOCKS_PER_SM;
 
 template <int WS>
 __device__ __forceinline__ uint4 realign(const uint4& lo, const uint4& hi, unsigned sh) {
@@ -115,16 +117,33 @@ __global__ void __launch_bounds__(kThreads, KI_COPY_MIN_BLOCKS) vcopy_kernel(Cop
     }
 }
 
-}  // namespace
+// Resident blocks per SM of one vcopy_kernel instantiation (queried once per context).
+template <int WS, bool ALIGNED>
+int resident_blocks(ki_ctx* ctx, int idx) {
+    if (ctx->copy_resident[idx] == 0) {
+        int r = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, vcopy_kernel<WS, ALIGNED>, kThreads, 0) != cudaSuccess ||
+            r < 1)
+            r = 1;
+        ctx->copy_resident[idx] = r;
+    }
+    return ctx->copy_resident[idx];
+}
 
-extern "C" int ki_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream) {
-    KI_CHECK_CTX(ctx);
-    if (nbytes == 0) return KI_OK;
-    if (!dst || !src) return ki::set_error(ctx, KI_ERR_ARG, "vcopy: null pointer");
+template <int WS, bool ALIGNED>
+int launch_one(ki_ctx* ctx, const CopyArgs& a, size_t want_blocks, int idx, cudaStream_t st) {
+    // Whole waves only: a grid that is not a multiple of the resident blocks leaves a partial last
+    // wave in which some SMs stream at a fraction of their occupancy.
+    const size_t wave = (size_t)ctx->sm_count * resident_blocks<WS, ALIGNED>(ctx, idx);
+    size_t blocks = wave * KI_COPY_WAVES;
+    if (want_blocks < blocks) blocks = want_blocks;
+    vcopy_kernel<WS, ALIGNED><<<(unsigned)blocks, kThreads, 0, st>>>(a);
+    return ki::check_launch(ctx, "vcopy_kernel launch");
+}
+
+// dst, src device pointers that do not overlap; nbytes > 0; device already current.
+int launch_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, cudaStream_t st) {
     const uintptr_t d0 = (uintptr_t)dst, s0 = (uintptr_t)src;
-    if (d0 < s0 + nbytes && s0 < d0 + nbytes)
-        return ki::set_error(ctx, KI_ERR_ARG, "vcopy: source and destination overlap");
-    KI_GUARD(ctx);
     CopyArgs a;
     a.dst = static_cast<uint8_t*>(dst);
     a.src = static_cast<const uint8_t*>(src);
@@ -137,16 +156,92 @@ extern "C" int ki_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, 
     a.src_al = reinterpret_cast<const uint4*>(sb - s);
     a.sh = (s & 3) * 8;
     const size_t nspans = (a.nchunks + kSpan - 1) / kSpan;
-    size_t blocks = (nspans + (kThreads / 32) - 1) / (kThreads / 32);
-    const size_t max_blocks = (size_t)ctx->sm_count * kBlocksPerSm;
-    if (blocks > max_blocks) blocks = max_blocks;
-    if (blocks < 1) blocks = 1;
-    cudaStream_t st = ki::as_stream(stream);
-    const dim3 g((unsigned)blocks), b(kThreads);
-    if (s == 0) vcopy_kernel<0, true><<<g, b, 0, st>>>(a);
-    else if (s < 4) vcopy_kernel<0, false><<<g, b, 0, st>>>(a);
-    else if (s < 8) vcopy_kernel<1, false><<<g, b, 0, st>>>(a);
-    else if (s < 12) vcopy_kernel<2, false><<<g, b, 0, st>>>(a);
-    else vcopy_kernel<3, false><<<g, b, 0, st>>>(a);
-    return ki::check_launch(ctx, "vcopy_kernel launch");
+    size_t want = (nspans + (kThreads / 32) - 1) / (kThreads / 32);
+    if (want < 1) want = 1;
+    if (s == 0) return launch_one<0, true>(ctx, a, want, 0, st);
+    if (s < 4) return launch_one<0, false>(ctx, a, want, 1, st);
+    if (s < 8) return launch_one<1, false>(ctx, a, want, 2, st);
+    if (s < 12) return launch_one<2, false>(ctx, a, want, 3, st);
+    return launch_one<3, false>(ctx, a, want, 4, st);
+}
+
+int ensure_pipe(ki_ctx* ctx) {
+    if (ctx->pipe_end) return KI_OK;
+    for (int i = 0; i < 3; ++i)
+        if (!ctx->pipe_stream[i])
+            KI_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->pipe_stream[i], cudaStreamNonBlocking));
+    for (int k = 0; k < KI_PIPE_SLOTS; ++k) {
+        if (!ctx->pipe_landed[k]) KI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->pipe_landed[k], cudaEventDisableTiming));
+        if (!ctx->pipe_copied[k]) KI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->pipe_copied[k], cudaEventDisableTiming));
+        if (!ctx->pipe_drained[k])
+            KI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->pipe_drained[k], cudaEventDisableTiming));
+    }
+    if (!ctx->pipe_begin) KI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->pipe_begin, cudaEventDisableTiming));
+    KI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->pipe_end, cudaEventDisableTiming));  // last: marks "complete"
+    return KI_OK;
+}
+
+bool overlap(uintptr_t d0, uintptr_t s0, size_t n) { return d0 < s0 + n && s0 < d0 + n; }
+
+}  // namespace
+
+extern "C" int ki_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream) {
+    KI_CHECK_CTX(ctx);
+    if (nbytes == 0) return KI_OK;
+    if (!dst || !src) return ki::set_error(ctx, KI_ERR_ARG, "vcopy: null pointer");
+    if (overlap((uintptr_t)dst, (uintptr_t)src, nbytes))
+        return ki::set_error(ctx, KI_ERR_ARG, "vcopy: source and destination overlap");
+    KI_GUARD(ctx);
+    return launch_vcopy(ctx, dst, src, nbytes, ki::as_stream(stream));
+}
+
+// Chunks of KI_PIPE_CHUNK bytes go host -> device on stream 0, are copied by vcopy_kernel on
+// stream 1 and come back on stream 2, cycling over KI_PIPE_SLOTS staging slots; events order the
+// three streams per slot, so both copy directions and the kernel run concurrently.  Inside each
+// slot a chunk keeps its host address modulo 16, so the kernel sees the caller's misalignment.
+extern "C" int ki_vcopy_host(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream) {
+    KI_CHECK_CTX(ctx);
+    if (nbytes == 0) return KI_OK;
+    if (!dst || !src) return ki::set_error(ctx, KI_ERR_ARG, "vcopy_host: null pointer");
+    if (overlap((uintptr_t)dst, (uintptr_t)src, nbytes))
+        return ki::set_error(ctx, KI_ERR_ARG, "vcopy_host: source and destination overlap");
+    KI_GUARD(ctx);
+    int rc = ensure_pipe(ctx);
+    if (rc) return rc;
+    constexpr size_t kChunk = KI_PIPE_CHUNK;
+    constexpr size_t kSlot = kChunk + 256;
+    void* stage = nullptr;
+    rc = ki::ensure_region(ctx, KI_REG_STAGE, 2 * KI_PIPE_SLOTS * kSlot, &stage);
+    if (rc) return rc;
+    cudaStream_t s = ki::as_stream(stream);
+    cudaStream_t up = ctx->pipe_stream[0], kern = ctx->pipe_stream[1], down = ctx->pipe_stream[2];
+    KI_CUDA(ctx, cudaEventRecord(ctx->pipe_begin, s));
+    for (int i = 0; i < 3; ++i) KI_CUDA(ctx, cudaStreamWaitEvent(ctx->pipe_stream[i], ctx->pipe_begin, 0));
+    const size_t so = (uintptr_t)src & 15, dso = (uintptr_t)dst & 15;
+    const uint8_t* hs = static_cast<const uint8_t*>(src);
+    uint8_t* hd = static_cast<uint8_t*>(dst);
+    uint8_t* base = static_cast<uint8_t*>(stage);
+    const size_t nch = (nbytes + kChunk - 1) / kChunk;
+    for (size_t i = 0; i < nch; ++i) {
+        const int k = (int)(i % KI_PIPE_SLOTS);
+        const size_t off = i * kChunk, len = (nbytes - off < kChunk) ? nbytes - off : kChunk;
+        uint8_t* in = base + (size_t)k * kSlot + so;
+        uint8_t* out = base + (size_t)(KI_PIPE_SLOTS + k) * kSlot + dso;
+        if (i >= (size_t)KI_PIPE_SLOTS) {
+            KI_CUDA(ctx, cudaStreamWaitEvent(up, ctx->pipe_copied[k], 0));     // input slot read
+            KI_CUDA(ctx, cudaStreamWaitEvent(kern, ctx->pipe_drained[k], 0));  // output slot sent back
+        }
+        KI_CUDA(ctx, cudaMemcpyAsync(in, hs + off, len, cudaMemcpyHostToDevice, up));
+        KI_CUDA(ctx, cudaEventRecord(ctx->pipe_landed[k], up));
+        KI_CUDA(ctx, cudaStreamWaitEvent(kern, ctx->pipe_landed[k], 0));
+        rc = launch_vcopy(ctx, out, in, len, kern);
+        if (rc) return rc;
+        KI_CUDA(ctx, cudaEventRecord(ctx->pipe_copied[k], kern));
+        KI_CUDA(ctx, cudaStreamWaitEvent(down, ctx->pipe_copied[k], 0));
+        KI_CUDA(ctx, cudaMemcpyAsync(hd + off, out, len, cudaMemcpyDeviceToHost, down));
+        KI_CUDA(ctx, cudaEventRecord(ctx->pipe_drained[k], down));
+    }
+    KI_CUDA(ctx, cudaEventRecord(ctx->pipe_end, down));
+    KI_CUDA(ctx, cudaStreamWaitEvent(s, ctx->pipe_end, 0));
+    return KI_OK;
 }

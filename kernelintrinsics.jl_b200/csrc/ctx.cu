@@ -82,6 +82,15 @@ int ki_ctx_destroy(ki_ctx* ctx) {
     {
         ki::DeviceGuard g(ctx->device);
         cudaDeviceSynchronize();
+        for (int i = 0; i < KI_PIPE_SLOTS; ++i) {
+            if (ctx->pipe_landed[i]) cudaEventDestroy(ctx->pipe_landed[i]);
+            if (ctx->pipe_copied[i]) cudaEventDestroy(ctx->pipe_copied[i]);
+            if (ctx->pipe_drained[i]) cudaEventDestroy(ctx->pipe_drained[i]);
+        }
+        if (ctx->pipe_begin) cudaEventDestroy(ctx->pipe_begin);
+        if (ctx->pipe_end) cudaEventDestroy(ctx->pipe_end);
+        for (int i = 0; i < 3; ++i)
+            if (ctx->pipe_stream[i]) cudaStreamDestroy(ctx->pipe_stream[i]);
         for (int r = 0; r < KI_REG_COUNT; ++r)
             if (ctx->region[r]) cudaFree(ctx->region[r]);
         if (ctx->d_status) cudaFree(ctx->d_status);

@@ -17,7 +17,17 @@ enum : uint32_t {
 };
 
 // Scratch regions, one per operation so different operations never share memory.
-enum ki_region { KI_REG_REDUCE = 0, KI_REG_SCAN = 1, KI_REG_COMPACT = 2, KI_REG_MISC = 3, KI_REG_COUNT = 4 };
+enum ki_region {
+    KI_REG_REDUCE = 0,
+    KI_REG_SCAN = 1,
+    KI_REG_COMPACT = 2,
+    KI_REG_MISC = 3,
+    KI_REG_STAGE = 4,  // device staging slots of the host-buffer copy
+    KI_REG_COUNT = 5
+};
+
+// Host-buffer copy pipeline: slots of staging memory cycled over three streams.
+constexpr int KI_PIPE_SLOTS = 4;
 
 struct ki_ctx {
     int device = 0;
@@ -29,6 +39,13 @@ struct ki_ctx {
     void* region[KI_REG_COUNT] = {};
     size_t region_bytes[KI_REG_COUNT] = {};
     char last_error[512] = {0};
+    int copy_resident[5] = {};  // resident vcopy blocks per SM, per instantiation
+    // host-buffer copy pipeline: streams [0] host -> device, [1] kernel, [2] device -> host
+    cudaStream_t pipe_stream[3] = {};
+    cudaEvent_t pipe_landed[KI_PIPE_SLOTS] = {};   // slot's input chunk is on the device
+    cudaEvent_t pipe_copied[KI_PIPE_SLOTS] = {};   // kernel finished: input read, output written
+    cudaEvent_t pipe_drained[KI_PIPE_SLOTS] = {};  // slot's output chunk is back in host memory
+    cudaEvent_t pipe_begin = nullptr, pipe_end = nullptr;
 };
 
 namespace ki {

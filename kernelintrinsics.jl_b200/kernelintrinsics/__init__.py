@@ -30,7 +30,7 @@ __all__ = [
     "Up", "Down", "Xor", "Idx", "All", "AnyLane", "Uni", "Ballot", "KIError", "KIArgumentError",
     "KITimeoutError", "Context", "context", "warpsize", "get_warpsize", "devices", "shfl", "warpreduce",
     "warpfold", "vote", "vload", "vstore", "vload_multi", "vstore_multi", "generate_partN", "access",
-    "message_pass", "vcopy", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
+    "message_pass", "vcopy", "vcopy_host", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
     "fp8_gemm", "fill_uniform", "fill_int_range", "fill_bytes", "fill_normal", "fill_e4m3_uniform",
 ]
 
@@ -422,6 +422,22 @@ def vcopy(dst, src, nbytes: Optional[int] = None, dst_offset: int = 0, src_offse
         raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy: range outside the tensors")
     context(d).call("ki_vcopy", ctypes.c_void_p(dst.data_ptr() + dst_offset),
                     ctypes.c_void_p(src.data_ptr() + src_offset), int(nbytes), _stream_ptr(stream, d))
+    return dst
+
+
+def vcopy_host(dst, src, nbytes: Optional[int] = None, dst_offset: int = 0, src_offset: int = 0, device: int = 0,
+               stream=None):
+    """copyto! between two host (CPU) tensors through device ``device``: chunks go to the device, are
+    copied by the vectorised copy kernel and come back, both directions overlapped.  Pinned host
+    tensors make the call asynchronous; it is complete when ``stream`` is."""
+    if dst.is_cuda or src.is_cuda:
+        raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_host: host tensors expected")
+    if nbytes is None:
+        nbytes = min(src.numel() * src.element_size() - src_offset, dst.numel() * dst.element_size() - dst_offset)
+    if src_offset + nbytes > src.numel() * src.element_size() or dst_offset + nbytes > dst.numel() * dst.element_size():
+        raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_host: range outside the tensors")
+    context(device).call("ki_vcopy_host", ctypes.c_void_p(dst.data_ptr() + dst_offset),
+                         ctypes.c_void_p(src.data_ptr() + src_offset), int(nbytes), _stream_ptr(stream, device))
     return dst
 
 

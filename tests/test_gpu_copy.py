@@ -82,3 +82,38 @@ def test_repeatable_on_streams(KI, dev):
             KI.vcopy(dst, src, src.numel() - 16, dst_offset=k, src_offset=15 - k)
             assert torch.equal(dst[k:k + src.numel() - 16], src[15 - k:15 - k + src.numel() - 16])
     s.synchronize()
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_buffers_pipelined(KI, oracle, dev, pinned):
+    """ki_vcopy_host: host -> device -> kernel -> host in overlapped chunks, any alignment, ragged
+    lengths around the chunk size; guard bytes of the host destination survive."""
+    import torch
+
+    chunk = 16 << 20  # KI_PIPE_CHUNK
+    n_max = 5 * chunk + 4096
+    src = torch.from_numpy(oracle.gen_bytes(7, n_max + 32))
+    if pinned:
+        src = src.pin_memory()
+    dst = torch.empty(n_max + 2 * GUARD + 32, dtype=torch.uint8, pin_memory=pinned)
+    s_np = src.numpy()
+    cases = [(0, 0, 1), (3, 11, 100), (5, 0, chunk - 1), (0, 7, chunk), (15, 1, chunk + 1),
+             (9, 9, 4 * chunk), (2, 13, 5 * chunk + 4095), (1, 0, 3 * chunk + 17)]
+    for so, do, n in cases:
+        dst.fill_(0xA5)
+        KI.vcopy_host(dst, src, n, dst_offset=GUARD + do, src_offset=so, device=dev.index or 0)
+        torch.cuda.current_stream(dev).synchronize()
+        got = dst.numpy()
+        assert np.array_equal(got[GUARD + do:GUARD + do + n], s_np[so:so + n]), (so, do, n)
+        assert (got[:GUARD + do] == 0xA5).all() and (got[GUARD + do + n:] == 0xA5).all(), (so, do, n)
+    KI.context(dev.index or 0).check()
+
+
+def test_host_buffers_rejects_device_and_overlap(KI, dev):
+    import torch
+
+    h = torch.zeros(1024, dtype=torch.uint8)
+    with pytest.raises(KI.KIArgumentError):
+        KI.vcopy_host(h, h, 100, dst_offset=50, src_offset=0)
+    with pytest.raises(KI.KIArgumentError):
+        KI.vcopy_host(h, torch.zeros(1024, dtype=torch.uint8, device=dev), 100)

@@ -43,9 +43,10 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of the
-# headline kernel; the capture and its command are summarised in profiles/.  None until captured.
+# headline kernel (ncu flushes L2 before the capture, so ~50 MB of the launch's writes are still in
+# L2 when it ends); the capture and its command are summarised in profiles/.
 NCU_TRAFFIC_PER_LAUNCH = {
-    "vcopy_kernel": None,
+    "vcopy_kernel": 486_999_808,
 }
 
 

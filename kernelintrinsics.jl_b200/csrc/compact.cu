@@ -44,16 +44,20 @@ namespace {
 #ifndef KI_COMPACT_CTAS_PER_SM
 #define KI_COMPACT_CTAS_PER_SM 3
 #endif
-constexpr int kWorkWarps = 8;
+#ifndef KI_COMPACT_WORK_WARPS
+#define KI_COMPACT_WORK_WARPS 8
+#endif
+constexpr int kWorkWarps = KI_COMPACT_WORK_WARPS;
 constexpr int kLookWarp = kWorkWarps;
 constexpr int kWorkThreads = 32 * kWorkWarps;
 constexpr int kThreads = kWorkThreads + 32;
 constexpr int kTile = KI_COMPACT_TILE;
 constexpr int kWarpSpan = kTile / kWorkWarps;   // elements per work warp
 constexpr int kRows = kWarpSpan / 128;          // rows of 32 lanes x float4
-static_assert(kWarpSpan % 128 == 0, "tile must split into rows of 128 elements per warp");
+static_assert(kWarpSpan % 128 == 0 && kWorkWarps <= 32, "tile must split into rows of 128 elements per warp");
 constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
-constexpr size_t kSmemBytes = kTile * sizeof(float);
+static_assert(kRows % kBatch == 0, "rows must split into whole batches");
+constexpr size_t kSmemBytes = (size_t)kTile * sizeof(float);
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 
@@ -81,6 +85,12 @@ struct Pending {
 
 __device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
 
+__device__ __forceinline__ int kept4(const float4& v, float thr) {
+    return (v.x > thr) + (v.y > thr) + (v.z > thr) + (v.w > thr);
+}
+
+// VALS / IDX: which outputs are written (an absent output costs no instructions).
+template <bool VALS, bool IDX>
 __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* sb = reinterpret_cast<float*>(smem_raw);
@@ -111,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
     __syncthreads();
 
     const unsigned below = (1u << lane) - 1u;  // lanes with a lower index
+    const float thr = a.thr;
     uint32_t phase = 0;
     bool have_old = false;
     int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
@@ -134,17 +145,14 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
                     ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
                 phase ^= 1u;
             } else {
-                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.x[first + i] : 0.0f;
+                // partial or unaligned tile: plain loads, padded with values that are never kept
+                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.x[first + i] : -INFINITY;
                 work_sync();
             }
+            const float4* row0 = reinterpret_cast<const float4*>(sb + w * kWarpSpan) + lane;
             int c = 0;
-#pragma unroll 4
-            for (int j = 0; j < kRows; ++j) {
-                const int i0 = w * kWarpSpan + 128 * j + 4 * (int)lane;
-                const float4 v = *reinterpret_cast<const float4*>(sb + i0);
-                c += (i0 + 0 < count && v.x > a.thr) + (i0 + 1 < count && v.y > a.thr) +
-                     (i0 + 2 < count && v.z > a.thr) + (i0 + 3 < count && v.w > a.thr);
-            }
+#pragma unroll 8
+            for (int j = 0; j < kRows; ++j) c += kept4(row0[32 * j], thr);
             c = ki::warpfold(c, ki::Add{});
             if (lane == 0) warp_cnt[w] = c;
             work_sync();
@@ -170,44 +178,41 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
             const size_t first = (size_t)o.t * kTile;
             const int count = (int)min((size_t)kTile, a.n - first);
             const bool vec_in = a.tma_in && count == kTile;
-            int64_t pos = o.tile_excl + o.warp_excl[w];
+            // outputs of this warp start at one pointer; offsets from it fit 32 bits
+            const int64_t at = o.tile_excl + o.warp_excl[w];
+            float* vals = VALS ? a.out_vals + at : nullptr;
+            int32_t* idxs = IDX ? a.out_idx + at : nullptr;
+            const int i_lane = w * kWarpSpan + 4 * (int)lane;                  // element of (row 0, q 0)
+            // output index of that element; unsigned, so the padding past the last element wraps
+            // harmlessly instead of overflowing (it is never stored)
+            const uint32_t ix0 = (uint32_t)((int64_t)first + a.index_base) + (uint32_t)i_lane;
+            int pos = 0;
+#pragma unroll 1
             for (int j0 = 0; j0 < kRows; j0 += kBatch) {
                 float4 v[kBatch];
 #pragma unroll
-                for (int j = 0; j < kBatch; ++j) {  // all loads in flight first
-                    const int i0 = w * kWarpSpan + 128 * (j0 + j) + 4 * (int)lane;
+                for (int j = 0; j < kBatch; ++j) {  // a batch of loads in flight first
+                    const int i0 = i_lane + 128 * (j0 + j);
                     if (vec_in) {
                         v[j] = KI_RELOAD(reinterpret_cast<const float4*>(a.x + first + i0));
                     } else {
-                        v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : 0.0f;
-                        v[j].y = (i0 + 1 < count) ? a.x[first + i0 + 1] : 0.0f;
-                        v[j].z = (i0 + 2 < count) ? a.x[first + i0 + 2] : 0.0f;
-                        v[j].w = (i0 + 3 < count) ? a.x[first + i0 + 3] : 0.0f;
+                        v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : -INFINITY;
+                        v[j].y = (i0 + 1 < count) ? a.x[first + i0 + 1] : -INFINITY;
+                        v[j].z = (i0 + 2 < count) ? a.x[first + i0 + 2] : -INFINITY;
+                        v[j].w = (i0 + 3 < count) ? a.x[first + i0 + 3] : -INFINITY;
                     }
                 }
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {
-                    const int i0 = w * kWarpSpan + 128 * (j0 + j) + 4 * (int)lane;
-                    const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-                    bool p[4];
-                    int rank = 0, row = 0;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        p[q] = (i0 + q < count) && e[q] > a.thr;
-                        const unsigned bal = ki::ballot(p[q]);
-                        rank += __popc(bal & below);
-                        row += __popc(bal);
-                    }
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (p[q]) {
-                            const int64_t o_at = pos + rank;
-                            if (a.out_vals) a.out_vals[o_at] = e[q];
-                            if (a.out_idx) a.out_idx[o_at] = (int32_t)((int64_t)(first + i0 + q) + a.index_base);
-                            ++rank;
-                        }
-                    }
-                    pos += row;
+                    const bool p0 = v[j].x > thr, p1 = v[j].y > thr, p2 = v[j].z > thr, p3 = v[j].w > thr;
+                    const unsigned b0 = ki::ballot(p0), b1 = ki::ballot(p1), b2 = ki::ballot(p2), b3 = ki::ballot(p3);
+                    int r = pos + __popc(b0 & below) + __popc(b1 & below) + __popc(b2 & below) + __popc(b3 & below);
+                    const uint32_t ix = ix0 + 128u * (uint32_t)(j0 + j);
+                    if (p0) { if (VALS) vals[r] = v[j].x; if (IDX) idxs[r] = (int32_t)ix; ++r; }
+                    if (p1) { if (VALS) vals[r] = v[j].y; if (IDX) idxs[r] = (int32_t)(ix + 1u); ++r; }
+                    if (p2) { if (VALS) vals[r] = v[j].z; if (IDX) idxs[r] = (int32_t)(ix + 2u); ++r; }
+                    if (p3) { if (VALS) vals[r] = v[j].w; if (IDX) idxs[r] = (int32_t)(ix + 3u); }
+                    pos += __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
                 }
             }
             if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);
@@ -216,6 +221,14 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         have_old = new_valid;
         cur ^= 1;
     }
+}
+
+template <bool VALS, bool IDX>
+int launch_compact(ki_ctx* ctx, const CompactArgs& a, size_t grid, cudaStream_t s) {
+    KI_CUDA(ctx, cudaFuncSetAttribute(compact_gt_f32_kernel<VALS, IDX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kSmemBytes));
+    compact_gt_f32_kernel<VALS, IDX><<<(unsigned)grid, kThreads, kSmemBytes, s>>>(a);
+    return ki::check_launch(ctx, "compact_gt_f32_kernel launch");
 }
 
 }  // namespace
@@ -242,8 +255,6 @@ extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float 
     if (rc) return rc;
     char* b = static_cast<char*>(base);
     KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * sizeof(uint64_t), s));
-    KI_CUDA(ctx, cudaFuncSetAttribute(compact_gt_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)kSmemBytes));
     CompactArgs a;
     a.x = d_x;
     a.n = n;
@@ -261,6 +272,8 @@ extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float 
     a.tma_in = ki::aligned(d_x, 16);
     size_t grid = (size_t)ctx->sm_count * kCtasPerSm;
     if (grid > ntiles) grid = ntiles;
-    compact_gt_f32_kernel<<<(unsigned)grid, kThreads, kSmemBytes, s>>>(a);
-    return ki::check_launch(ctx, "compact_gt_f32_kernel launch");
+    if (d_out_vals && d_out_idx) return launch_compact<true, true>(ctx, a, grid, s);
+    if (d_out_vals) return launch_compact<true, false>(ctx, a, grid, s);
+    if (d_out_idx) return launch_compact<false, true>(ctx, a, grid, s);
+    return launch_compact<false, false>(ctx, a, grid, s);
 }

@@ -1,10 +1,10 @@
 // scan.cu -- single-pass decoupled-lookback inclusive scan of Int64 (Base.cumsum semantics).
 //
-// Persistent CTAs, software-pipelined over tiles of 4096 elements, with 8 "work" warps and one
-// "look" warp.  Iteration k of a CTA runs two phases:
-//   phase A  work warps: wait for tile k (one 32 KiB 1-D TMA bulk copy, cp.async.bulk ...
+// One persistent CTA per SM, software-pipelined over tiles of 15360 elements, with 30 "work" warps
+// and one "look" warp (992 threads).  Iteration k of a CTA runs two phases:
+//   phase A  work warps: wait for tile k (one 120 KiB 1-D TMA bulk copy, cp.async.bulk ...
 //            mbarrier::complete_tx), sum it (warp w folds its 512 elements with @warpfold over 8 rows
-//            of 32 lanes x 2 elements; warp 0 scans the 8 warp totals with @warpreduce) and publish
+//            of 32 lanes x 2 elements; warp 0 scans the 30 warp totals with @warpreduce) and publish
 //            its aggregate at once (ki/lookback.cuh: packed 64-bit status word, st.release.gpu);
 //            look warp, at the same time: the decoupled lookback of tile k-1;
 //   phase B  the look warp takes the next ticket and starts its TMA into the (now free) tile buffer;
@@ -16,6 +16,12 @@
 // ~1 us L2 round trips of a lookback overlap the next tile's load and first pass.  Tile indices
 // come from an atomic ticket, so a tile's predecessors are always taken by CTAs that already run.
 // Tiles that are partial or not 16-byte aligned are staged with plain loads.
+//
+// Why one large CTA per SM: a lookback costs L2 round trips in proportion to the number of tiles
+// in flight ahead of it, and a tile's bytes set how long its CTA has before the next one; few, large
+// tiles keep the lookback inside the pipeline, and 30 warps keep enough loads in flight.  Measured
+// at n = 2^30: 4096-element tiles x 3 CTAs/SM 0.78 of HBM peak, 8192 x 2 0.82, 12288 x 1 (24 warps)
+// 0.88, 15360 x 1 (30 warps) 0.92.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
@@ -34,19 +40,27 @@
 
 namespace {
 
-constexpr int kWorkWarps = 8;
+#ifndef KI_SCAN_TILE
+#define KI_SCAN_TILE 15360
+#endif
+#ifndef KI_SCAN_WORK_WARPS
+#define KI_SCAN_WORK_WARPS 30
+#endif
+constexpr int kWorkWarps = KI_SCAN_WORK_WARPS;
 constexpr int kLookWarp = kWorkWarps;
 constexpr int kWorkThreads = 32 * kWorkWarps;
 constexpr int kThreads = kWorkThreads + 32;
-constexpr int kTile = 4096;                     // elements per tile
-constexpr int kWarpSpan = kTile / kWorkWarps;   // 512 elements per work warp
-constexpr int kRows = kWarpSpan / 64;           // 8 rows of 32 lanes x 2 elements
+constexpr int kTile = KI_SCAN_TILE;             // elements per tile
+constexpr int kWarpSpan = kTile / kWorkWarps;   // elements per work warp (512)
+constexpr int kRows = kWarpSpan / 64;           // rows of 32 lanes x 2 elements
+static_assert(kWarpSpan % 64 == 0 && kWorkWarps <= 32, "tile must split into rows of 64 elements per warp");
+constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
 constexpr size_t kSmemBytes = kTile * sizeof(int64_t);
 #ifndef KI_SCAN_LOOKBACK_K
 #define KI_SCAN_LOOKBACK_K 1
 #endif
 #ifndef KI_SCAN_CTAS_PER_SM
-#define KI_SCAN_CTAS_PER_SM 3
+#define KI_SCAN_CTAS_PER_SM 1
 #endif
 constexpr int kLookbackK = KI_SCAN_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_SCAN_CTAS_PER_SM;
@@ -161,31 +175,34 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
             const int count = (int)min((size_t)kTile, a.n - first);
             const bool full = count == kTile;
             int64_t carry = ki::wrap_add(o.tile_excl, o.warp_excl[w]);
-            longlong2 v[kRows];
 #pragma unroll
-            for (int j = 0; j < kRows; ++j) {  // all loads in flight before the scan
-                const int i = w * kWarpSpan + 64 * j + 2 * (int)lane;
-                if (full && a.tma_in) {
-                    v[j] = KI_RELOAD(reinterpret_cast<const longlong2*>(a.in + first + i));
-                } else {
-                    v[j].x = (i < count) ? a.in[first + i] : 0;
-                    v[j].y = (i + 1 < count) ? a.in[first + i + 1] : 0;
-                }
-            }
+            for (int j0 = 0; j0 < kRows; j0 += kBatch) {
+                longlong2 v[kBatch];
 #pragma unroll
-            for (int j = 0; j < kRows; ++j) {
-                const int64_t pair = ki::wrap_add(v[j].x, v[j].y);
-                const int64_t inc = ki::warpreduce(pair, ki::WrapAdd{});
-                const int64_t o0 = ki::wrap_add(ki::wrap_add(carry, ki::wrap_sub(inc, pair)), v[j].x);
-                const int64_t o1 = ki::wrap_add(o0, v[j].y);
-                const int i = w * kWarpSpan + 64 * j + 2 * (int)lane;
-                if (full && a.vec_out) {
-                    __stcs(reinterpret_cast<longlong2*>(a.out + first + i), make_longlong2(o0, o1));
-                } else {
-                    if (i < count) a.out[first + i] = o0;
-                    if (i + 1 < count) a.out[first + i + 1] = o1;
+                for (int jj = 0; jj < kBatch; ++jj) {  // a batch of loads in flight before the scan
+                    const int i = w * kWarpSpan + 64 * (j0 + jj) + 2 * (int)lane;
+                    if (full && a.tma_in) {
+                        v[jj] = KI_RELOAD(reinterpret_cast<const longlong2*>(a.in + first + i));
+                    } else {
+                        v[jj].x = (i < count) ? a.in[first + i] : 0;
+                        v[jj].y = (i + 1 < count) ? a.in[first + i + 1] : 0;
+                    }
                 }
-                carry = ki::wrap_add(carry, __shfl_sync(0xffffffffu, inc, 31));
+#pragma unroll
+                for (int jj = 0; jj < kBatch; ++jj) {
+                    const int64_t pair = ki::wrap_add(v[jj].x, v[jj].y);
+                    const int64_t inc = ki::warpreduce(pair, ki::WrapAdd{});
+                    const int64_t o0 = ki::wrap_add(ki::wrap_add(carry, ki::wrap_sub(inc, pair)), v[jj].x);
+                    const int64_t o1 = ki::wrap_add(o0, v[jj].y);
+                    const int i = w * kWarpSpan + 64 * (j0 + jj) + 2 * (int)lane;
+                    if (full && a.vec_out) {
+                        __stcs(reinterpret_cast<longlong2*>(a.out + first + i), make_longlong2(o0, o1));
+                    } else {
+                        if (i < count) a.out[first + i] = o0;
+                        if (i + 1 < count) a.out[first + i + 1] = o1;
+                    }
+                    carry = ki::wrap_add(carry, __shfl_sync(0xffffffffu, inc, 31));
+                }
             }
         }
         __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
@@ -256,8 +273,8 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
 // same kernel as ki_scan_inclusive_i64 but takes its tile-status scratch from the file-scope array
 // below instead of a context, so it needs no context and allocates nothing.
 //
-// The array is sized for KI_SCAN_NOALLOC_MAX_N elements (65,536 tiles: a 256-byte header plus three
-// 8-byte words per tile, about 1.5 MiB).  Every GPU that loads this library holds it until the
+// The array is sized for KI_SCAN_NOALLOC_MAX_N elements (a 256-byte header plus three 8-byte words
+// per tile: 17,477 tiles of 15360 elements, about 410 KiB).  Every GPU that loads this library holds it until the
 // process exits.  In host code the array's name is only a host-side stand-in, so its device address
 // is looked up once per device with cudaGetSymbolAddress (with that device current) and cached; the
 // first call on each device does this set-up and must therefore come before any stream capture.

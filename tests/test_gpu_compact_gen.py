@@ -43,6 +43,37 @@ def test_compact_edge_values(KI, oracle, dev):
     assert c.item() == 10000 and torch.equal(i.cpu(), torch.arange(1, 10001, dtype=torch.int32))
 
 
+def test_compact_single_output_and_top_index(KI, oracle, dev):
+    """Values only and indices only (null output pointers through the C ABI), and indices that end
+    exactly at typemax(Int32)."""
+    import ctypes
+
+    import torch
+
+    n = 3 * 16384 + 999
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    KI.fill_normal(x, seed=9)
+    host = x.cpu().numpy()
+    ctx = KI.context(0)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    for index_base in (1, 2**31 - n):
+        rv, ri = oracle.filter_gt_f32(host, 0.5, index_base=index_base)
+        vals = torch.full((n,), -7.0, dtype=torch.float32, device=dev)
+        idx = torch.full((n,), -7, dtype=torch.int32, device=dev)
+        cnt = torch.zeros((), dtype=torch.uint64, device=dev)
+        ctx.call("ki_compact_gt_f32", ctypes.c_void_p(x.data_ptr()), n, ctypes.c_float(0.5),
+                 ctypes.c_void_p(vals.data_ptr()), None, ctypes.c_int64(index_base), ctypes.c_void_p(cnt.data_ptr()),
+                 stream)
+        ctx.call("ki_compact_gt_f32", ctypes.c_void_p(x.data_ptr()), n, ctypes.c_float(0.5), None,
+                 ctypes.c_void_p(idx.data_ptr()), ctypes.c_int64(index_base), None, stream)
+        ctx.check()
+        k = rv.size
+        assert cnt.item() == k
+        assert np.array_equal(vals[:k].cpu().numpy(), rv) and (vals[k:] == -7.0).all().item()
+        assert np.array_equal(idx[:k].cpu().numpy(), ri) and (idx[k:] == -7).all().item()
+    assert ri[-1] <= 2**31 - 1
+
+
 def test_compact_rejects_index_overflow(KI, dev):
     import torch
 

@@ -124,7 +124,7 @@ int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size
  * hosts whose device memory belongs to another allocator, loops that forbid allocation after
  * start-up.  Same result as ki_scan_inclusive_i64, but needs no context and calls no cudaMalloc,
  * cudaFree or allocating routine: its tile-status scratch is a static device array sized for
- * n <= KI_SCAN_NOALLOC_MAX_N (about 410 KiB, held by every GPU that loads the library until exit).
+ * n <= KI_SCAN_NOALLOC_MAX_N (about 400 KiB, held by every GPU that loads the library until exit).
  * n beyond that returns KI_ERR_ARG.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress, with that device current): make it before any stream capture.
  * Every call shares the array; calls that overlap on the GPU race.  Uses the current device. */

@@ -32,6 +32,10 @@
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
 
+#ifndef KI_GEMM_PAIRS
+#define KI_GEMM_PAIRS 1  // use the CTA-pair kernel where M and N are multiples of 256
+#endif
+
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4, ACCS = 2;
@@ -337,6 +341,270 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// CTA-pair variant: cluster of 2 CTAs on 2 SMs, 256 x 256 output tiles, tcgen05.mma.cta_group::2.
+//
+// CTA rank r of the pair loads A rows [m0 + 128 r, +128) and B columns [n0 + 128 r, +128) of each
+// K block into its own shared memory (no multicast: every CTA loads only its own half).  Both CTAs'
+// loads complete on the full barrier of rank 0 (.cta_group::2 lets the peer's copy signal it), and
+// rank 0's MMA thread issues M=256 N=256 K=32 MMAs that read A and B from both CTAs' shared memory
+// at the same offsets; each CTA's TMEM receives its 128 rows x 256 columns.  Per SM this moves
+// 32 KiB per K block for a 128 x 256 x 128 product instead of 48 KiB, so six stages fit and the
+// shared-memory ingress per flop falls by a third.  The MMA thread's commits arrive on the empty /
+// accumulator-full barriers of both CTAs (one commit per CTA); the epilogue warps of both CTAs
+// arrive on rank 0's accumulator-empty barrier.
+// ---------------------------------------------------------------------------------------------
+constexpr int STAGES2 = 6;
+constexpr int STAGE2_BYTES = A_BYTES + B_HALF_BYTES;  // 32 KiB per CTA
+constexpr int RING2_BYTES = STAGES2 * STAGE2_BYTES;
+constexpr int SMEM2_BYTES = 1024 + RING2_BYTES + EPI_BYTES + BAR_BYTES;
+constexpr uint32_t IDESC2 = (1u << 4)             // D = F32
+                            | (0u << 7) | (0u << 10)  // A, B = e4m3
+                            | (0u << 15)          // A K-major
+                            | (1u << 16)          // B MN-major
+                            | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Tile load into this CTA's shared memory whose completion is counted on `bar_cluster`, a barrier
+// of either CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(bar_cluster)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(IDESC2), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive (once) on a barrier of either CTA when all earlier pair MMAs of this thread are done.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_e4m3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmC, int M, int N, int K, float alpha,
+                          uint32_t* status, uint64_t timeout_ns) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw = ki::smem_addr(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;  // identical in both CTAs: same kernel, same layout
+    const uint32_t ring = base;
+    const uint32_t epi = base + RING2_BYTES;
+    const uint32_t bars = epi + EPI_BYTES;
+    const uint32_t full0 = bars, empty0 = bars + 8 * STAGES2, tfull0 = bars + 16 * STAGES2;
+    const uint32_t tempty0 = tfull0 + 8 * ACCS;
+    const uint32_t drain = tempty0 + 8 * ACCS;
+    uint8_t* gbase = smem_raw + (base - raw);
+    const int misc = RING2_BYTES + EPI_BYTES + 16 * STAGES2 + 16 * ACCS + 8;
+    volatile int* abort = reinterpret_cast<volatile int*>(gbase + misc);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + misc + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES2; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(full0 + 8 * s));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(empty0 + 8 * s));
+        }
+        for (int b = 0; b < ACCS; ++b) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tfull0 + 8 * b));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty0 + 8 * b), "r"(2 * EPI_WARPS));
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(drain));
+        *abort = 0;
+        ki::fence_mbar_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
+    }
+    if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM together
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         ki::smem_addr(tmem_holder)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers are initialised before any copy or arrive crosses over
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    const int num_m = M / 256, num_n = N / 256, tiles = num_m * num_n, kblocks = K / BK;
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full_lead0 = map_rank(full0, 0);
+            int s = 0;
+            uint32_t ph = 1;  // a fresh barrier's preceding phase counts as complete
+            uint32_t issued_ph[STAGES2];
+            bool issued[STAGES2];
+            for (int k = 0; k < STAGES2; ++k) issued[k] = false;
+            for (int tile = pair; tile < tiles && !*abort; tile += pairs) {
+                const int m0 = (tile % num_m) * 256 + 128 * (int)rank, n0 = (tile / num_m) * 256 + 128 * (int)rank;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!wait_bar(empty0 + 8 * s, ph, abort, status, timeout_ns)) break;
+                    const uint32_t sa = ring + s * STAGE2_BYTES, sb = sa + A_BYTES;
+                    if (leader) mbar_expect_tx(full0 + 8 * s, 2 * STAGE2_BYTES);  // both CTAs' bytes
+                    tma_load_2d_pair(sa, &tmA, kb * BK, m0, full_lead0 + 8 * s);
+                    tma_load_2d_pair(sb, &tmB, n0, kb * BK, full_lead0 + 8 * s);
+                    issued[s] = true;
+                    issued_ph[s] = ph ^ 1;
+                    if (++s == STAGES2) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            if (*abort) {
+                if (leader) {  // loads may still be in flight into both CTAs: wait (bounded) for them
+                    for (int k = 0; k < STAGES2; ++k)
+                        if (issued[k]) wait_drain(full0 + 8 * k, issued_ph[k], status, timeout_ns);
+                } else {  // this CTA cannot observe rank 0's barrier: give its last loads time to land
+                    const uint64_t t0 = ki::globaltimer_ns();
+                    while (ki::globaltimer_ns() - t0 < 200000ull) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            const uint32_t empty_peer0 = map_rank(empty0, 1), tfull_peer0 = map_rank(tfull0, 1);
+            int s = 0, acc = 0;
+            uint32_t ph_full = 0, ph_empty = 1;
+            for (int tile = pair; tile < tiles && !*abort; tile += pairs) {
+                if (!wait_bar(tempty0 + 8 * acc, ph_empty, abort, status, timeout_ns)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * BN);
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!wait_bar(full0 + 8 * s, ph_full, abort, status, timeout_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = ring + s * STAGE2_BYTES, sb = sa + A_BYTES;
+                    const uint64_t adesc = make_desc(sa, 16, 1024);
+                    const uint64_t bdesc = make_desc(sb, B_HALF_BYTES, 1024);
+#pragma unroll
+                    for (int k = 0; k < BK / 32; ++k)
+                        mma_f8_pair(d, adesc + (uint64_t)((k * 32) >> 4), bdesc + (uint64_t)((k * 32 * 128) >> 4),
+                                    (kb | k) != 0);
+                    mma_commit_pair(empty0 + 8 * s);       // this CTA's stage is free again
+                    mma_commit_pair(empty_peer0 + 8 * s);  // and the peer's
+                    if (++s == STAGES2) {
+                        s = 0;
+                        ph_full ^= 1;
+                    }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull0 + 8 * acc);
+                mma_commit_pair(tfull_peer0 + 8 * acc);
+                if (++acc == ACCS) {
+                    acc = 0;
+                    ph_empty ^= 1;
+                }
+            }
+            mma_commit_pair(drain);  // every MMA issued has finished before TMEM and the rings go
+            wait_drain(drain, 0, status, timeout_ns);
+        }
+    } else {
+        const int ew = warp - 2;  // epilogue warp 0..3
+        const int q = warp & 3;   // TMEM lane quadrant this warp may access
+        const int row0 = q * 32;
+        const uint32_t tempty_lead0 = map_rank(tempty0, 0);
+        int acc = 0, buf = 0;
+        uint32_t ph = 0;
+        for (int tile = pair; tile < tiles; tile += pairs) {
+            const int m0 = (tile % num_m) * 256 + 128 * (int)rank, n0 = (tile / num_m) * 256;
+            int ok = 0;
+            if (lane == 0) ok = wait_bar(tfull0 + 8 * acc, ph, abort, status, timeout_ns) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BN / EPI_COLS; ++c) {
+                uint32_t v[32];
+                const uint32_t taddr = tmem + ((uint32_t)row0 << 16) + (uint32_t)(acc * BN + c * EPI_COLS);
+                KI_TMEM_LD_X32(taddr, v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (c == BN / EPI_COLS - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(tempty_lead0 + 8 * acc);
+                }
+                if (lane == 0) bulk_wait_read_le1();
+                __syncwarp();
+                const uint32_t sbuf = epi + (uint32_t)((ew * 2 + buf) * EPI_BUF_BYTES);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t addr = sbuf + (uint32_t)lane * 128u + (uint32_t)(((j ^ (lane & 7)) << 4));
+                    const float f0 = __uint_as_float(v[4 * j + 0]) * alpha, f1 = __uint_as_float(v[4 * j + 1]) * alpha;
+                    const float f2 = __uint_as_float(v[4 * j + 2]) * alpha, f3 = __uint_as_float(v[4 * j + 3]) * alpha;
+                    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(f0), "f"(f1), "f"(f2),
+                                 "f"(f3)
+                                 : "memory");
+                }
+                ki::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmC, n0 + c * EPI_COLS, m0 + row0, sbuf);
+                    ki::bulk_commit();
+                }
+                buf ^= 1;
+            }
+            if (++acc == ACCS) {
+                acc = 0;
+                ph ^= 1;
+            }
+        }
+        if (lane == 0) ki::bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // neither CTA leaves while the other may still read its shared memory or TMEM
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -384,10 +652,43 @@ extern "C" int ki_gemm_e4m3_f32(ki_ctx* ctx, const uint8_t* d_A, const uint8_t* 
         !encode_2d(enc, &tC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d_C, (uint64_t)N, (uint64_t)M, (uint64_t)N * 4, EPI_COLS,
                    32, CU_TENSOR_MAP_L2_PROMOTION_NONE))
         return ki::set_error(ctx, KI_ERR_ARG, "gemm: tensor map encoding failed");
+    cudaStream_t st = ki::as_stream(stream);
+    const float alpha = scale_a * scale_b;
+    if (M % 256 == 0 && N % 256 == 0 && KI_GEMM_PAIRS) {
+        // CTA pairs: grid = as many pairs as can be resident at once (persistent), at most one per tile
+        KI_CUDA(ctx, cudaFuncSetAttribute(gemm_e4m3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          SMEM2_BYTES));
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = SMEM2_BYTES;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (ctx->gemm_pairs == 0) {
+            int nc = 0;
+            cfg.gridDim = dim3(2 * (ctx->sm_count / 2));
+            if (cudaOccupancyMaxActiveClusters(&nc, gemm_e4m3_pair_kernel, &cfg) != cudaSuccess || nc < 1) {
+                cudaGetLastError();
+                nc = ctx->sm_count / 2;
+            }
+            ctx->gemm_pairs = nc;
+        }
+        const int tiles = (M / 256) * (N / 256);
+        const int pairs = tiles < ctx->gemm_pairs ? tiles : ctx->gemm_pairs;
+        cfg.gridDim = dim3(2 * pairs);
+        KI_CUDA(ctx, cudaLaunchKernelEx(&cfg, gemm_e4m3_pair_kernel, tA, tB, tC, M, N, K, alpha, ctx->d_status,
+                                        ctx->wait_timeout_ns));
+        return ki::check_launch(ctx, "gemm_e4m3_pair_kernel launch");
+    }
     KI_CUDA(ctx, cudaFuncSetAttribute(gemm_e4m3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     const int tiles = (M / BM) * (N / BN);
     const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-    gemm_e4m3_kernel<<<grid, THREADS, SMEM_BYTES, ki::as_stream(stream)>>>(tA, tB, tC, M, N, K, scale_a * scale_b,
-                                                                         ctx->d_status, ctx->wait_timeout_ns);
+    gemm_e4m3_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(tA, tB, tC, M, N, K, alpha, ctx->d_status,
+                                                        ctx->wait_timeout_ns);
     return ki::check_launch(ctx, "gemm_e4m3_kernel launch");
 }

@@ -40,6 +40,7 @@ struct ki_ctx {
     size_t region_bytes[KI_REG_COUNT] = {};
     char last_error[512] = {0};
     int copy_resident[5] = {};  // resident vcopy blocks per SM, per instantiation
+    int gemm_pairs = 0;         // co-resident CTA pairs of the pair GEMM kernel
     // host-buffer copy pipeline: streams [0] host -> device, [1] kernel, [2] device -> host
     cudaStream_t pipe_stream[3] = {};
     cudaEvent_t pipe_landed[KI_PIPE_SLOTS] = {};   // slot's input chunk is on the device

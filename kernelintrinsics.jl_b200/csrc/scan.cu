@@ -1,10 +1,10 @@
 // scan.cu -- single-pass decoupled-lookback inclusive scan of Int64 (Base.cumsum semantics).
 //
-// One persistent CTA per SM, software-pipelined over tiles of 15360 elements, with 30 "work" warps
-// and one "look" warp (992 threads).  Iteration k of a CTA runs two phases:
-//   phase A  work warps: wait for tile k (one 120 KiB 1-D TMA bulk copy, cp.async.bulk ...
+// One persistent CTA per SM, software-pipelined over tiles of 15872 elements, with 31 "work" warps
+// and one "look" warp (1024 threads).  Iteration k of a CTA runs two phases:
+//   phase A  work warps: wait for tile k (one 124 KiB 1-D TMA bulk copy, cp.async.bulk ...
 //            mbarrier::complete_tx), sum it (warp w folds its 512 elements with @warpfold over 8 rows
-//            of 32 lanes x 2 elements; warp 0 scans the 30 warp totals with @warpreduce) and publish
+//            of 32 lanes x 2 elements; warp 0 scans the 31 warp totals with @warpreduce) and publish
 //            its aggregate at once (ki/lookback.cuh: packed 64-bit status word, st.release.gpu);
 //            look warp, at the same time: the decoupled lookback of tile k-1;
 //   phase B  the look warp takes the next ticket and starts its TMA into the (now free) tile buffer;
@@ -21,7 +21,7 @@
 // in flight ahead of it, and a tile's bytes set how long its CTA has before the next one; few, large
 // tiles keep the lookback inside the pipeline, and 30 warps keep enough loads in flight.  Measured
 // at n = 2^30: 4096-element tiles x 3 CTAs/SM 0.78 of HBM peak, 8192 x 2 0.82, 12288 x 1 (24 warps)
-// 0.88, 15360 x 1 (30 warps) 0.92.
+// 0.88, 15360 x 1 (30 warps) 0.92, 15872 x 1 (31 warps) 0.94.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
@@ -41,10 +41,10 @@
 namespace {
 
 #ifndef KI_SCAN_TILE
-#define KI_SCAN_TILE 15360
+#define KI_SCAN_TILE 15872
 #endif
 #ifndef KI_SCAN_WORK_WARPS
-#define KI_SCAN_WORK_WARPS 30
+#define KI_SCAN_WORK_WARPS 31
 #endif
 constexpr int kWorkWarps = KI_SCAN_WORK_WARPS;
 constexpr int kLookWarp = kWorkWarps;
@@ -274,8 +274,8 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
 // below instead of a context, so it needs no context and allocates nothing.
 //
 // The array is sized for KI_SCAN_NOALLOC_MAX_N elements (a 256-byte header plus three 8-byte words
-// per tile: 17,477 tiles of 15360 elements, about 410 KiB).  Every GPU that loads this library holds it until the
-// process exits.  In host code the array's name is only a host-side stand-in, so its device address
+// per tile: 16,913 tiles of 15872 elements, about 397 KiB).  Every GPU that loads this library
+// holds it until the process exits.  In host code the array's name is only a host-side stand-in, so its device address
 // is looked up once per device with cudaGetSymbolAddress (with that device current) and cached; the
 // first call on each device does this set-up and must therefore come before any stream capture.
 // All calls share the array and it keeps the last call's contents: each call clears the ticket, the

@@ -65,7 +65,7 @@ def test_reduce_i64_vs_oracle(KI, oracle, dev, n):
         assert KI.reduce_sum_i64(xs).item() == oracle.sum_i64(xs.cpu().numpy())
 
 
-@pytest.mark.parametrize("n", [1, 2, 3, 31, 32, 4095, 4096, 4097, 8192, 12289, 15359, 15360, 15361, 30721,
+@pytest.mark.parametrize("n", [1, 2, 3, 31, 32, 4095, 4096, 4097, 8192, 12289, 15871, 15872, 15873, 31745,
                                (1 << 16) + 3, (1 << 22) + 5])
 def test_scan_vs_oracle(KI, oracle, dev, n):
     import torch
@@ -84,7 +84,7 @@ def test_scan_vs_oracle(KI, oracle, dev, n):
 def test_scan_misaligned_and_in_place(KI, oracle, dev):
     import torch
 
-    n = 3 * 15360 + 17
+    n = 3 * 15872 + 17
     base = torch.empty(n + 1, dtype=torch.int64, device=dev)
     KI.fill_int_range(base, seed=9, lo=-5, hi=5)
     x = base[1:]  # 8 mod 16: the plain-load path
@@ -97,7 +97,7 @@ def test_scan_misaligned_and_in_place(KI, oracle, dev):
 def test_scan_wraps_like_int64(KI, oracle, dev):
     import torch
 
-    host = np.full(3 * 15360 + 5, 2**61 + 12345, dtype=np.int64)
+    host = np.full(3 * 15872 + 5, 2**61 + 12345, dtype=np.int64)
     host[::7] = -(2**62)
     x = torch.from_numpy(host).to(dev)
     assert np.array_equal(KI.warpreduce_scan(x).cpu().numpy(), oracle.cumsum_i64(host))

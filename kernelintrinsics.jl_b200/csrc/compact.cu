@@ -57,7 +57,16 @@ constexpr int kRows = kWarpSpan / 128;          // rows of 32 lanes x float4
 static_assert(kWarpSpan % 128 == 0 && kWorkWarps <= 32, "tile must split into rows of 128 elements per warp");
 constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
 static_assert(kRows % kBatch == 0, "rows must split into whole batches");
-constexpr size_t kSmemBytes = (size_t)kTile * sizeof(float);
+#ifndef KI_COMPACT_ST_CS
+#define KI_COMPACT_ST_CS 1  // streaming (evict-first) stores of the output
+#endif
+#ifndef KI_COMPACT_STAGE
+#define KI_COMPACT_STAGE 1  // kept elements of a row go through a per-warp shared-memory run
+#endif
+// per warp: 128 values + 32 discard slots, then 128 indices + 32 discard slots
+constexpr int kStageSlots = 160;
+constexpr size_t kStageBytes = KI_COMPACT_STAGE ? (size_t)kWorkWarps * kStageSlots * 8 : 0;
+constexpr size_t kSmemBytes = (size_t)kTile * sizeof(float) + kStageBytes;
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 
@@ -109,8 +118,8 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         ticket = t;
         if (bulk_ok(t)) {
             ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
-            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kSmemBytes);
-            KI_G2S(sb, a.x + t * kTile, (uint32_t)kSmemBytes, &bar);
+            ki::mbar_arrive_expect_tx(&bar, (uint32_t)(kTile * sizeof(float)));
+            KI_G2S(sb, a.x + t * kTile, (uint32_t)(kTile * sizeof(float)), &bar);
         }
     };
     if (tid == 0) {
@@ -187,6 +196,10 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
             // harmlessly instead of overflowing (it is never stored)
             const uint32_t ix0 = (uint32_t)((int64_t)first + a.index_base) + (uint32_t)i_lane;
             int pos = 0;
+#if KI_COMPACT_STAGE
+            float* sv = reinterpret_cast<float*>(smem_raw + (size_t)kTile * sizeof(float)) + w * 2 * kStageSlots;
+            int32_t* si = reinterpret_cast<int32_t*>(sv + kStageSlots);
+#endif
 #pragma unroll 1
             for (int j0 = 0; j0 < kRows; j0 += kBatch) {
                 float4 v[kBatch];
@@ -206,13 +219,46 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
                 for (int j = 0; j < kBatch; ++j) {
                     const bool p0 = v[j].x > thr, p1 = v[j].y > thr, p2 = v[j].z > thr, p3 = v[j].w > thr;
                     const unsigned b0 = ki::ballot(p0), b1 = ki::ballot(p1), b2 = ki::ballot(p2), b3 = ki::ballot(p3);
-                    int r = pos + __popc(b0 & below) + __popc(b1 & below) + __popc(b2 & below) + __popc(b3 & below);
+                    const int ahead = __popc(b0 & below) + __popc(b1 & below) + __popc(b2 & below) + __popc(b3 & below);
+                    const int row = __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
                     const uint32_t ix = ix0 + 128u * (uint32_t)(j0 + j);
+#if KI_COMPACT_STAGE
+                    // the row's kept elements, in source order, as one run in this warp's stage (an
+                    // element that is not kept goes to the lane's discard slot: no branches) ...
+                    const int r0 = ahead, r1 = r0 + (int)p0, r2 = r1 + (int)p1, r3 = r2 + (int)p2;
+                    const int junk = 128 + (int)lane;
+                    if (VALS) {
+                        sv[p0 ? r0 : junk] = v[j].x;
+                        sv[p1 ? r1 : junk] = v[j].y;
+                        sv[p2 ? r2 : junk] = v[j].z;
+                        sv[p3 ? r3 : junk] = v[j].w;
+                    }
+                    if (IDX) {
+                        si[p0 ? r0 : junk] = (int32_t)ix;
+                        si[p1 ? r1 : junk] = (int32_t)(ix + 1u);
+                        si[p2 ? r2 : junk] = (int32_t)(ix + 2u);
+                        si[p3 ? r3 : junk] = (int32_t)(ix + 3u);
+                    }
+                    __syncwarp();
+                    // ... written out with consecutive lanes on consecutive addresses
+                    for (int e = (int)lane; e < row; e += 32) {
+#if KI_COMPACT_ST_CS
+                        if (VALS) __stcs(vals + pos + e, sv[e]);
+                        if (IDX) __stcs(idxs + pos + e, si[e]);
+#else
+                        if (VALS) vals[pos + e] = sv[e];
+                        if (IDX) idxs[pos + e] = si[e];
+#endif
+                    }
+                    __syncwarp();
+#else
+                    int r = pos + ahead;
                     if (p0) { if (VALS) vals[r] = v[j].x; if (IDX) idxs[r] = (int32_t)ix; ++r; }
                     if (p1) { if (VALS) vals[r] = v[j].y; if (IDX) idxs[r] = (int32_t)(ix + 1u); ++r; }
                     if (p2) { if (VALS) vals[r] = v[j].z; if (IDX) idxs[r] = (int32_t)(ix + 2u); ++r; }
                     if (p3) { if (VALS) vals[r] = v[j].w; if (IDX) idxs[r] = (int32_t)(ix + 3u); }
-                    pos += __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
+#endif
+                    pos += row;
                 }
             }
             if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);

@@ -21,11 +21,13 @@
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
 
-// Tiles are read twice: once by TMA for the first pass, once from L2 for the second.
-#ifndef KI_KEEP_TILES
-#define KI_KEEP_TILES 1
+// Tiles are read twice: once by TMA for the first pass, once from L2 for the second (brought back
+// by an L2 bulk prefetch while the tile's prefix is looked up).  With the prefetch, marking the
+// first read evict-last costs more than it saves, so by default it is a plain bulk load.
+#ifndef KI_COMPACT_KEEP_TILES
+#define KI_COMPACT_KEEP_TILES 0
 #endif
-#if KI_KEEP_TILES
+#if KI_COMPACT_KEEP_TILES
 #define KI_G2S ki::bulk_g2s_keep
 #define KI_RELOAD(p) __ldcs(p)
 #else
@@ -57,6 +59,9 @@ constexpr int kRows = kWarpSpan / 128;          // rows of 32 lanes x float4
 static_assert(kWarpSpan % 128 == 0 && kWorkWarps <= 32, "tile must split into rows of 128 elements per warp");
 constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
 static_assert(kRows % kBatch == 0, "rows must split into whole batches");
+#ifndef KI_COMPACT_PREFETCH
+#define KI_COMPACT_PREFETCH 1  // L2 prefetch of tile k-1 before its second pass
+#endif
 #ifndef KI_COMPACT_ST_CS
 #define KI_COMPACT_ST_CS 1  // streaming (evict-first) stores of the output
 #endif
@@ -66,7 +71,13 @@ static_assert(kRows % kBatch == 0, "rows must split into whole batches");
 // per warp: 128 values + 32 discard slots, then 128 indices + 32 discard slots
 constexpr int kStageSlots = 160;
 constexpr size_t kStageBytes = KI_COMPACT_STAGE ? (size_t)kWorkWarps * kStageSlots * 8 : 0;
-constexpr size_t kSmemBytes = (size_t)kTile * sizeof(float) + kStageBytes;
+#ifndef KI_COMPACT_BUFS
+#define KI_COMPACT_BUFS 1  // 1: the second pass re-reads the tile from L2; 3: tiles k-1, k, k+1 in smem
+#endif                     // 2: as 1, and tile k+1's load starts at the top of iteration k
+constexpr int kBufs = KI_COMPACT_BUFS;
+static_assert(kBufs >= 1 && kBufs <= 3, "one, two or three tile buffers");
+constexpr size_t kTileBytes = (size_t)kTile * sizeof(float);
+constexpr size_t kSmemBytes = kBufs * kTileBytes + kStageBytes;
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 
@@ -103,46 +114,61 @@ template <bool VALS, bool IDX>
 __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* sb = reinterpret_cast<float*>(smem_raw);
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bars[2];
     __shared__ int warp_cnt[kWorkWarps];
     __shared__ Pending slot[2];  // tile k (being counted) and tile k-1 (being written)
-    __shared__ unsigned long long ticket;
+    __shared__ unsigned long long tickets[2];
 
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
     const uint64_t ntiles = (a.n + kTile - 1) / kTile;
     auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
-    auto fetch = [&]() {  // take a ticket and start its load (one thread)
+    // take a ticket into tickets[ts] and start its load into buffer `buf` (one thread)
+    auto fetch = [&](int buf, int ts) {
         const unsigned long long t = atomicAdd(a.ticket, 1ull);
-        ticket = t;
+        tickets[ts] = t;
         if (bulk_ok(t)) {
-            ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
-            ki::mbar_arrive_expect_tx(&bar, (uint32_t)(kTile * sizeof(float)));
-            KI_G2S(sb, a.x + t * kTile, (uint32_t)(kTile * sizeof(float)), &bar);
+            uint64_t* bar = &bars[kBufs == 2 ? buf : 0];
+            ki::fence_proxy_async_smem();  // earlier generic reads of the buffer come first
+            ki::mbar_arrive_expect_tx(bar, (uint32_t)kTileBytes);
+            KI_G2S(sb + (size_t)buf * kTile, a.x + t * kTile, (uint32_t)kTileBytes, bar);
         }
     };
     if (tid == 0) {
-        ki::mbar_init(&bar, 1);
+        ki::mbar_init(&bars[0], 1);
+        ki::mbar_init(&bars[1], 1);
         ki::fence_mbar_init();
-        fetch();
+        fetch(0, 0);
     }
     __syncthreads();
 
     const unsigned below = (1u << lane) - 1u;  // lanes with a lower index
     const float thr = a.thr;
-    uint32_t phase = 0;
+    uint32_t phases = 0;  // bit b: parity of bars[b]'s next phase
     bool have_old = false;
     int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
+    int buf = 0;  // buffer of tile k; with three buffers tile k-1 is in (buf + 2) % 3
+    int ts = 0;   // tickets[] entry of tile k (two buffers: alternates)
     while (true) {
-        const uint64_t t_new = ticket;
+        const uint64_t t_new = tickets[ts];
+        float* tb = sb + (size_t)buf * kTile;
         const bool new_valid = t_new < ntiles;
         if (!new_valid && !have_old) break;
+        if (kBufs == 2 && tid == kLookWarp * 32) {  // tile k+1's load starts now, into the other buffer
+            if (new_valid) fetch(buf ^ 1, ts ^ 1);
+            else tickets[ts ^ 1] = ~0ull;
+        }
 
         // ---- phase A: count and publish tile k  ||  look back for tile k-1 -------------------------
         if (w == kLookWarp) {
             if (have_old) {
                 Pending& o = slot[cur ^ 1];
+#if KI_COMPACT_PREFETCH
+                // bring tile k-1 back into L2 (if it left) while its prefix is looked up
+                if (kBufs != 3 && lane == 0 && a.tma_in && (o.t + 1) * (uint64_t)kTile <= a.n)
+                    ki::bulk_prefetch_l2(a.x + o.t * kTile, (uint32_t)kTileBytes);
+#endif
                 const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, 0, a.status, a.timeout_ns);
                 if (lane == 0) o.tile_excl = ex;
             }
@@ -150,15 +176,17 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
             const size_t first = (size_t)t_new * kTile;
             const int count = (int)min((size_t)kTile, a.n - first);
             if (bulk_ok(t_new)) {
-                if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
-                    ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
-                phase ^= 1u;
+                const int bi = kBufs == 2 ? buf : 0;
+                const uint32_t par = (phases >> bi) & 1u;
+                if (!ki::mbar_wait_bounded(&bars[bi], par, a.status, a.timeout_ns))
+                    ki::mbar_wait_bounded(&bars[bi], par, a.status, a.timeout_ns);  // never leave a copy in flight
+                phases ^= 1u << bi;
             } else {
                 // partial or unaligned tile: plain loads, padded with values that are never kept
-                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.x[first + i] : -INFINITY;
+                for (int i = tid; i < kTile; i += kWorkThreads) tb[i] = (i < count) ? a.x[first + i] : -INFINITY;
                 work_sync();
             }
-            const float4* row0 = reinterpret_cast<const float4*>(sb + w * kWarpSpan) + lane;
+            const float4* row0 = reinterpret_cast<const float4*>(tb + w * kWarpSpan) + lane;
             int c = 0;
 #pragma unroll 8
             for (int j = 0; j < kRows; ++j) c += kept4(row0[32 * j], thr);
@@ -181,7 +209,8 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         __syncthreads();  // tile k counted (buffer free, slot written); tile k-1's prefix known
 
         // ---- phase B: start tile k+1's load; write tile k-1 -------------------------------------------
-        if (tid == kLookWarp * 32 && new_valid) fetch();  // the look warp is idle in phase B
+        const int buf_next = (kBufs == 1) ? 0 : (buf + 1) % kBufs;
+        if (kBufs != 2 && tid == kLookWarp * 32 && new_valid) fetch(buf_next, 0);  // look warp is idle in B
         if (w < kWorkWarps && have_old) {
             const Pending& o = slot[cur ^ 1];
             const size_t first = (size_t)o.t * kTile;
@@ -197,7 +226,7 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
             const uint32_t ix0 = (uint32_t)((int64_t)first + a.index_base) + (uint32_t)i_lane;
             int pos = 0;
 #if KI_COMPACT_STAGE
-            float* sv = reinterpret_cast<float*>(smem_raw + (size_t)kTile * sizeof(float)) + w * 2 * kStageSlots;
+            float* sv = reinterpret_cast<float*>(smem_raw + kBufs * kTileBytes) + w * 2 * kStageSlots;
             int32_t* si = reinterpret_cast<int32_t*>(sv + kStageSlots);
 #endif
 #pragma unroll 1
@@ -206,7 +235,9 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {  // a batch of loads in flight first
                     const int i0 = i_lane + 128 * (j0 + j);
-                    if (vec_in) {
+                    if (kBufs == 3) {  // tile k-1 is still in its buffer, padded past count
+                        v[j] = *reinterpret_cast<const float4*>(sb + (size_t)((buf + 2) % 3) * kTile + i0);
+                    } else if (vec_in) {
                         v[j] = KI_RELOAD(reinterpret_cast<const float4*>(a.x + first + i0));
                     } else {
                         v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : -INFINITY;
@@ -266,6 +297,8 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
         have_old = new_valid;
         cur ^= 1;
+        buf = buf_next;
+        if (kBufs == 2) ts ^= 1;
     }
 }
 

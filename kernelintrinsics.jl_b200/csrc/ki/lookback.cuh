@@ -215,6 +215,11 @@ __device__ __forceinline__ void bulk_g2s_keep(void* dst_smem, const void* src_gm
         : "memory");
 }
 
+// Asynchronous prefetch of [src, src + bytes) into L2 (src 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src_gmem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes) : "memory");
+}
+
 // shared -> global bulk copy in the current bulk group.
 __device__ __forceinline__ void bulk_s2g(void* dst_gmem, const void* src_smem, uint32_t bytes) {
     asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem),

@@ -6,34 +6,30 @@
 //            mbarrier::complete_tx) and count its kept elements (warp w owns 2048 elements as 16 rows
 //            of 32 lanes x float4: conflict-free 16-byte shared loads); warp 0 scans the 8 warp
 //            counts with @warpreduce and publishes the tile count at once (ki/lookback.cuh);
-//            look warp, at the same time: the decoupled lookback of tile k-1;
+//            look warp, at the same time: an L2 bulk prefetch of tile k-1 (cp.async.bulk.prefetch)
+//            and the decoupled lookback of tile k-1;
 //   phase B  the look warp takes the next ticket and starts its TMA into the free buffer;
-//            work warps write tile k-1: re-read it from global memory (still in the 126 MB L2) and,
-//            for each row and component c, take a @vote Ballot (ext/CUDA/shuffle_vote.jl:23-34,
-//            vote.sync ballot -> UInt32).  An element's rank inside its row is
+//            work warps write tile k-1: re-read it from global memory (L2) and, for each row and
+//            component c, take a @vote Ballot (ext/CUDA/shuffle_vote.jl:23-34, vote.sync ballot ->
+//            UInt32).  An element's rank inside its row is
 //                sum over c of popc(ballot_c & lanes_below) + (kept components before it in its lane)
-//            which keeps source order (lane-major, then component); kept values and their indices
-//            are stored at tile prefix + warp prefix + row prefix + rank.
+//            which keeps source order (lane-major, then component).  The row's kept values and
+//            indices go to a per-warp shared-memory run at their ranks (an element that is not kept
+//            goes to its lane's discard slot, so there are no branches) and leave as coalesced
+//            evict-first stores at tile prefix + warp prefix + row prefix.
 // Between taking a ticket and publishing that tile's count a CTA only waits for its own load and
 // its own second pass, never for a lookback.  Tiles that are partial or not 16-byte aligned are read
-// with plain loads.
+// with plain loads (padded with -Inf, which is never kept).
+//
+// Measured at n = 2^28 (0.467 ms, 0.57 of the copy peak): without the stores the same kernel takes
+// 0.235 ms.  Writing the output streams evicts tiles that wait for their prefix, so most second-pass
+// reads come back from DRAM; the prefetch turns them into one asynchronous bulk read per tile
+// (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read, tiles
+// kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-element tiles, one or
+// two CTAs per SM with more warps, looking tile k up right after its count, early tickets.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
-
-// Tiles are read twice: once by TMA for the first pass, once from L2 for the second (brought back
-// by an L2 bulk prefetch while the tile's prefix is looked up).  With the prefetch, marking the
-// first read evict-last costs more than it saves, so by default it is a plain bulk load.
-#ifndef KI_COMPACT_KEEP_TILES
-#define KI_COMPACT_KEEP_TILES 0
-#endif
-#if KI_COMPACT_KEEP_TILES
-#define KI_G2S ki::bulk_g2s_keep
-#define KI_RELOAD(p) __ldcs(p)
-#else
-#define KI_G2S ki::bulk_g2s
-#define KI_RELOAD(p) (*(p))
-#endif
 
 namespace {
 
@@ -59,25 +55,11 @@ constexpr int kRows = kWarpSpan / 128;          // rows of 32 lanes x float4
 static_assert(kWarpSpan % 128 == 0 && kWorkWarps <= 32, "tile must split into rows of 128 elements per warp");
 constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
 static_assert(kRows % kBatch == 0, "rows must split into whole batches");
-#ifndef KI_COMPACT_PREFETCH
-#define KI_COMPACT_PREFETCH 1  // L2 prefetch of tile k-1 before its second pass
-#endif
-#ifndef KI_COMPACT_ST_CS
-#define KI_COMPACT_ST_CS 1  // streaming (evict-first) stores of the output
-#endif
-#ifndef KI_COMPACT_STAGE
-#define KI_COMPACT_STAGE 1  // kept elements of a row go through a per-warp shared-memory run
-#endif
 // per warp: 128 values + 32 discard slots, then 128 indices + 32 discard slots
 constexpr int kStageSlots = 160;
-constexpr size_t kStageBytes = KI_COMPACT_STAGE ? (size_t)kWorkWarps * kStageSlots * 8 : 0;
-#ifndef KI_COMPACT_BUFS
-#define KI_COMPACT_BUFS 1  // 1: the second pass re-reads the tile from L2; 3: tiles k-1, k, k+1 in smem
-#endif                     // 2: as 1, and tile k+1's load starts at the top of iteration k
-constexpr int kBufs = KI_COMPACT_BUFS;
-static_assert(kBufs >= 1 && kBufs <= 3, "one, two or three tile buffers");
+constexpr size_t kStageBytes = (size_t)kWorkWarps * kStageSlots * 8;
 constexpr size_t kTileBytes = (size_t)kTile * sizeof(float);
-constexpr size_t kSmemBytes = kBufs * kTileBytes + kStageBytes;
+constexpr size_t kSmemBytes = kTileBytes + kStageBytes;
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 
@@ -111,64 +93,51 @@ __device__ __forceinline__ int kept4(const float4& v, float thr) {
 
 // VALS / IDX: which outputs are written (an absent output costs no instructions).
 template <bool VALS, bool IDX>
-__global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(CompactArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* sb = reinterpret_cast<float*>(smem_raw);
-    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ __align__(8) uint64_t bar;
     __shared__ int warp_cnt[kWorkWarps];
     __shared__ Pending slot[2];  // tile k (being counted) and tile k-1 (being written)
-    __shared__ unsigned long long tickets[2];
+    __shared__ unsigned long long ticket;
 
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
     const uint64_t ntiles = (a.n + kTile - 1) / kTile;
     auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
-    // take a ticket into tickets[ts] and start its load into buffer `buf` (one thread)
-    auto fetch = [&](int buf, int ts) {
+    auto fetch = [&]() {  // take a ticket and start its load (one thread)
         const unsigned long long t = atomicAdd(a.ticket, 1ull);
-        tickets[ts] = t;
+        ticket = t;
         if (bulk_ok(t)) {
-            uint64_t* bar = &bars[kBufs == 2 ? buf : 0];
-            ki::fence_proxy_async_smem();  // earlier generic reads of the buffer come first
-            ki::mbar_arrive_expect_tx(bar, (uint32_t)kTileBytes);
-            KI_G2S(sb + (size_t)buf * kTile, a.x + t * kTile, (uint32_t)kTileBytes, bar);
+            ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
+            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kTileBytes);
+            ki::bulk_g2s(sb, a.x + t * kTile, (uint32_t)kTileBytes, &bar);
         }
     };
     if (tid == 0) {
-        ki::mbar_init(&bars[0], 1);
-        ki::mbar_init(&bars[1], 1);
+        ki::mbar_init(&bar, 1);
         ki::fence_mbar_init();
-        fetch(0, 0);
+        fetch();
     }
     __syncthreads();
 
     const unsigned below = (1u << lane) - 1u;  // lanes with a lower index
     const float thr = a.thr;
-    uint32_t phases = 0;  // bit b: parity of bars[b]'s next phase
+    uint32_t phase = 0;
     bool have_old = false;
     int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
-    int buf = 0;  // buffer of tile k; with three buffers tile k-1 is in (buf + 2) % 3
-    int ts = 0;   // tickets[] entry of tile k (two buffers: alternates)
     while (true) {
-        const uint64_t t_new = tickets[ts];
-        float* tb = sb + (size_t)buf * kTile;
+        const uint64_t t_new = ticket;
         const bool new_valid = t_new < ntiles;
         if (!new_valid && !have_old) break;
-        if (kBufs == 2 && tid == kLookWarp * 32) {  // tile k+1's load starts now, into the other buffer
-            if (new_valid) fetch(buf ^ 1, ts ^ 1);
-            else tickets[ts ^ 1] = ~0ull;
-        }
 
-        // ---- phase A: count and publish tile k  ||  look back for tile k-1 -------------------------
+        // ---- phase A: count and publish tile k  ||  prefetch and look back for tile k-1 ------------
         if (w == kLookWarp) {
             if (have_old) {
                 Pending& o = slot[cur ^ 1];
-#if KI_COMPACT_PREFETCH
                 // bring tile k-1 back into L2 (if it left) while its prefix is looked up
-                if (kBufs != 3 && lane == 0 && a.tma_in && (o.t + 1) * (uint64_t)kTile <= a.n)
-                    ki::bulk_prefetch_l2(a.x + o.t * kTile, (uint32_t)kTileBytes);
-#endif
+                if (lane == 0 && bulk_ok(o.t)) ki::bulk_prefetch_l2(a.x + o.t * kTile, (uint32_t)kTileBytes);
                 const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, 0, a.status, a.timeout_ns);
                 if (lane == 0) o.tile_excl = ex;
             }
@@ -176,17 +145,15 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
             const size_t first = (size_t)t_new * kTile;
             const int count = (int)min((size_t)kTile, a.n - first);
             if (bulk_ok(t_new)) {
-                const int bi = kBufs == 2 ? buf : 0;
-                const uint32_t par = (phases >> bi) & 1u;
-                if (!ki::mbar_wait_bounded(&bars[bi], par, a.status, a.timeout_ns))
-                    ki::mbar_wait_bounded(&bars[bi], par, a.status, a.timeout_ns);  // never leave a copy in flight
-                phases ^= 1u << bi;
+                if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
+                    ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
+                phase ^= 1u;
             } else {
                 // partial or unaligned tile: plain loads, padded with values that are never kept
-                for (int i = tid; i < kTile; i += kWorkThreads) tb[i] = (i < count) ? a.x[first + i] : -INFINITY;
+                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.x[first + i] : -INFINITY;
                 work_sync();
             }
-            const float4* row0 = reinterpret_cast<const float4*>(tb + w * kWarpSpan) + lane;
+            const float4* row0 = reinterpret_cast<const float4*>(sb + w * kWarpSpan) + lane;
             int c = 0;
 #pragma unroll 8
             for (int j = 0; j < kRows; ++j) c += kept4(row0[32 * j], thr);
@@ -209,8 +176,7 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         __syncthreads();  // tile k counted (buffer free, slot written); tile k-1's prefix known
 
         // ---- phase B: start tile k+1's load; write tile k-1 -------------------------------------------
-        const int buf_next = (kBufs == 1) ? 0 : (buf + 1) % kBufs;
-        if (kBufs != 2 && tid == kLookWarp * 32 && new_valid) fetch(buf_next, 0);  // look warp is idle in B
+        if (tid == kLookWarp * 32 && new_valid) fetch();  // the look warp is idle in phase B
         if (w < kWorkWarps && have_old) {
             const Pending& o = slot[cur ^ 1];
             const size_t first = (size_t)o.t * kTile;
@@ -220,25 +186,21 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
             const int64_t at = o.tile_excl + o.warp_excl[w];
             float* vals = VALS ? a.out_vals + at : nullptr;
             int32_t* idxs = IDX ? a.out_idx + at : nullptr;
-            const int i_lane = w * kWarpSpan + 4 * (int)lane;                  // element of (row 0, q 0)
+            const int i_lane = w * kWarpSpan + 4 * (int)lane;  // element of (row 0, component 0)
             // output index of that element; unsigned, so the padding past the last element wraps
             // harmlessly instead of overflowing (it is never stored)
             const uint32_t ix0 = (uint32_t)((int64_t)first + a.index_base) + (uint32_t)i_lane;
-            int pos = 0;
-#if KI_COMPACT_STAGE
-            float* sv = reinterpret_cast<float*>(smem_raw + kBufs * kTileBytes) + w * 2 * kStageSlots;
+            float* sv = reinterpret_cast<float*>(smem_raw + kTileBytes) + w * 2 * kStageSlots;
             int32_t* si = reinterpret_cast<int32_t*>(sv + kStageSlots);
-#endif
+            int pos = 0;
 #pragma unroll 1
             for (int j0 = 0; j0 < kRows; j0 += kBatch) {
                 float4 v[kBatch];
 #pragma unroll
                 for (int j = 0; j < kBatch; ++j) {  // a batch of loads in flight first
                     const int i0 = i_lane + 128 * (j0 + j);
-                    if (kBufs == 3) {  // tile k-1 is still in its buffer, padded past count
-                        v[j] = *reinterpret_cast<const float4*>(sb + (size_t)((buf + 2) % 3) * kTile + i0);
-                    } else if (vec_in) {
-                        v[j] = KI_RELOAD(reinterpret_cast<const float4*>(a.x + first + i0));
+                    if (vec_in) {
+                        v[j] = *reinterpret_cast<const float4*>(a.x + first + i0);
                     } else {
                         v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : -INFINITY;
                         v[j].y = (i0 + 1 < count) ? a.x[first + i0 + 1] : -INFINITY;
@@ -253,9 +215,7 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
                     const int ahead = __popc(b0 & below) + __popc(b1 & below) + __popc(b2 & below) + __popc(b3 & below);
                     const int row = __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
                     const uint32_t ix = ix0 + 128u * (uint32_t)(j0 + j);
-#if KI_COMPACT_STAGE
-                    // the row's kept elements, in source order, as one run in this warp's stage (an
-                    // element that is not kept goes to the lane's discard slot: no branches) ...
+                    // the row's kept elements, in source order, as one run in this warp's stage ...
                     const int r0 = ahead, r1 = r0 + (int)p0, r2 = r1 + (int)p1, r3 = r2 + (int)p2;
                     const int junk = 128 + (int)lane;
                     if (VALS) {
@@ -273,22 +233,10 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
                     __syncwarp();
                     // ... written out with consecutive lanes on consecutive addresses
                     for (int e = (int)lane; e < row; e += 32) {
-#if KI_COMPACT_ST_CS
                         if (VALS) __stcs(vals + pos + e, sv[e]);
                         if (IDX) __stcs(idxs + pos + e, si[e]);
-#else
-                        if (VALS) vals[pos + e] = sv[e];
-                        if (IDX) idxs[pos + e] = si[e];
-#endif
                     }
                     __syncwarp();
-#else
-                    int r = pos + ahead;
-                    if (p0) { if (VALS) vals[r] = v[j].x; if (IDX) idxs[r] = (int32_t)ix; ++r; }
-                    if (p1) { if (VALS) vals[r] = v[j].y; if (IDX) idxs[r] = (int32_t)(ix + 1u); ++r; }
-                    if (p2) { if (VALS) vals[r] = v[j].z; if (IDX) idxs[r] = (int32_t)(ix + 2u); ++r; }
-                    if (p3) { if (VALS) vals[r] = v[j].w; if (IDX) idxs[r] = (int32_t)(ix + 3u); }
-#endif
                     pos += row;
                 }
             }
@@ -297,8 +245,6 @@ __global__ void __launch_bounds__(kThreads) compact_gt_f32_kernel(CompactArgs a)
         __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
         have_old = new_valid;
         cur ^= 1;
-        buf = buf_next;
-        if (kBufs == 2) ts ^= 1;
     }
 }
 

@@ -2,7 +2,9 @@
 //
 // C (M x N, Float32, row-major) = alpha * A (M x K, e4m3, row-major) * B (K x N, e4m3, row-major)
 //
-// Persistent kernel, one CTA of 6 warps per SM, 128 x 256 output tiles, K blocks of 128:
+// Two persistent kernels.  gemm_e4m3_pair_kernel (further down) runs when M and N are multiples of
+// 256: clusters of two CTAs share 256 x 256 tiles through tcgen05.mma.cta_group::2.  Otherwise
+// gemm_e4m3_kernel, one CTA of 6 warps per SM, 128 x 256 output tiles, K blocks of 128:
 //   warp 0     TMA producer: 2-D tiled bulk-tensor loads (128B swizzle) of A (128 x 128 B, K-major)
 //              and B (2 x 128 K-rows x 128 B, N-major) into a 4-stage shared-memory ring;
 //   warp 1     allocates 512 TMEM columns (two 128 x 256 Float32 accumulators) and issues
@@ -373,21 +375,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 // loads complete on the full barrier of rank 0 (.cta_group::2 lets the peer's copy signal it), and
 // rank 0's MMA thread issues M=256 N=256 K=32 MMAs that read A and B from both CTAs' shared memory
 // at the same offsets; each CTA's TMEM receives its 128 rows x 256 columns.  Per SM this moves
-// 32 KiB per K block for a 128 x 256 x 128 product instead of 48 KiB, so seven stages fit and the
-// shared-memory ingress per flop falls by a third.  The epilogue stores straight from registers
-// (each lane owns one output row: 128 contiguous bytes per 32 columns), leaving all shared memory
-// to the ring.  The MMA thread's commits arrive on the empty /
+// 32 KiB per K block for a 128 x 256 x 128 product instead of 48 KiB, so six stages fit beside the
+// epilogue staging and the shared-memory ingress per flop falls by a third.  (Storing the epilogue
+// straight from registers to free a seventh stage was slower: 2472 against 2633 TFLOP/s.)  The MMA thread's commits arrive on the empty /
 // accumulator-full barriers of both CTAs (one commit per CTA); the epilogue warps of both CTAs
 // arrive on rank 0's accumulator-empty barrier.
 // ---------------------------------------------------------------------------------------------
-#ifndef KI_GEMM_PAIR_TMA_EPI
-#define KI_GEMM_PAIR_TMA_EPI 1  // 1: epilogue through shared memory + TMA stores; 0: from registers
-#endif
-constexpr int PAIR_EPI_BYTES = KI_GEMM_PAIR_TMA_EPI ? EPI_BYTES : 0;
-constexpr int STAGES2 = KI_GEMM_PAIR_TMA_EPI ? 6 : 7;
+constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_BYTES + B_HALF_BYTES;  // 32 KiB per CTA
 constexpr int RING2_BYTES = STAGES2 * STAGE2_BYTES;
-constexpr int SMEM2_BYTES = 1024 + RING2_BYTES + PAIR_EPI_BYTES + BAR_BYTES;
+constexpr int SMEM2_BYTES = 1024 + RING2_BYTES + EPI_BYTES + BAR_BYTES;
 constexpr uint32_t IDESC2 = (1u << 4)             // D = F32
                             | (0u << 7) | (0u << 10)  // A, B = e4m3
                             | (0u << 15)          // A K-major
@@ -443,19 +440,19 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_e4m3_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                          const __grid_constant__ CUtensorMap tmC, float* __restrict__ C, int M, int N, int K,
-                          float alpha, uint32_t* status, uint64_t timeout_ns) {
+                          const __grid_constant__ CUtensorMap tmC, int M, int N, int K, float alpha,
+                          uint32_t* status, uint64_t timeout_ns) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = ki::smem_addr(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // identical in both CTAs: same kernel, same layout
     const uint32_t ring = base;
     const uint32_t epi = base + RING2_BYTES;
-    const uint32_t bars = epi + PAIR_EPI_BYTES;
+    const uint32_t bars = epi + EPI_BYTES;
     const uint32_t full0 = bars, empty0 = bars + 8 * STAGES2, tfull0 = bars + 16 * STAGES2;
     const uint32_t tempty0 = tfull0 + 8 * ACCS;
     const uint32_t drain = tempty0 + 8 * ACCS;
     uint8_t* gbase = smem_raw + (base - raw);
-    const int misc = RING2_BYTES + PAIR_EPI_BYTES + 16 * STAGES2 + 16 * ACCS + 8;
+    const int misc = RING2_BYTES + EPI_BYTES + 16 * STAGES2 + 16 * ACCS + 8;
     volatile int* abort = reinterpret_cast<volatile int*>(gbase + misc);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(gbase + misc + 8);
 
@@ -478,7 +475,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ki::fence_mbar_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
-        if (KI_GEMM_PAIR_TMA_EPI) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmC) : "memory");
     }
     if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM together
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -590,7 +587,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            float* crow = C + (size_t)(m0 + row0 + lane) * (size_t)N + n0;  // this lane's output row
 #pragma unroll 1
             for (int c = 0; c < BN / EPI_COLS; ++c) {
                 uint32_t v[32];
@@ -602,40 +598,32 @@ __global__ void __launch_bounds__(THREADS, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(tempty_lead0 + 8 * acc);
                 }
-                if (KI_GEMM_PAIR_TMA_EPI) {
-                    if (lane == 0) bulk_wait_read_le1();
-                    __syncwarp();
-                    const uint32_t sbuf = epi + (uint32_t)((ew * 2 + buf) * EPI_BUF_BYTES);
+                if (lane == 0) bulk_wait_read_le1();
+                __syncwarp();
+                const uint32_t sbuf = epi + (uint32_t)((ew * 2 + buf) * EPI_BUF_BYTES);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t addr = sbuf + (uint32_t)lane * 128u + (uint32_t)(((j ^ (lane & 7)) << 4));
-                        const float f0 = __uint_as_float(v[4 * j + 0]) * alpha, f1 = __uint_as_float(v[4 * j + 1]) * alpha;
-                        const float f2 = __uint_as_float(v[4 * j + 2]) * alpha, f3 = __uint_as_float(v[4 * j + 3]) * alpha;
-                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(f0), "f"(f1), "f"(f2),
-                                     "f"(f3)
-                                     : "memory");
-                    }
-                    ki::fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmC, n0 + c * EPI_COLS, m0 + row0, sbuf);
-                        ki::bulk_commit();
-                    }
-                    buf ^= 1;
-                } else {
-                    float4* dst = reinterpret_cast<float4*>(crow + c * EPI_COLS);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        __stcs(dst + j, make_float4(__uint_as_float(v[4 * j + 0]) * alpha, __uint_as_float(v[4 * j + 1]) * alpha,
-                                                    __uint_as_float(v[4 * j + 2]) * alpha, __uint_as_float(v[4 * j + 3]) * alpha));
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t addr = sbuf + (uint32_t)lane * 128u + (uint32_t)(((j ^ (lane & 7)) << 4));
+                    const float f0 = __uint_as_float(v[4 * j + 0]) * alpha, f1 = __uint_as_float(v[4 * j + 1]) * alpha;
+                    const float f2 = __uint_as_float(v[4 * j + 2]) * alpha, f3 = __uint_as_float(v[4 * j + 3]) * alpha;
+                    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(f0), "f"(f1), "f"(f2),
+                                 "f"(f3)
+                                 : "memory");
                 }
+                ki::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmC, n0 + c * EPI_COLS, m0 + row0, sbuf);
+                    ki::bulk_commit();
+                }
+                buf ^= 1;
             }
             if (++acc == ACCS) {
                 acc = 0;
                 ph ^= 1;
             }
         }
-        if (KI_GEMM_PAIR_TMA_EPI && lane == 0) ki::bulk_wait_all();
+        if (lane == 0) ki::bulk_wait_all();
     }
 
     tc_fence_before();
@@ -724,8 +712,8 @@ extern "C" int ki_gemm_e4m3_f32(ki_ctx* ctx, const uint8_t* d_A, const uint8_t* 
         const int tiles = (M / 256) * (N / 256);
         const int pairs = tiles < ctx->gemm_pairs ? tiles : ctx->gemm_pairs;
         cfg.gridDim = dim3(2 * pairs);
-        KI_CUDA(ctx, cudaLaunchKernelEx(&cfg, gemm_e4m3_pair_kernel, tA, tB, tC, d_C, M, N, K, alpha,
-                                        ctx->d_status, ctx->wait_timeout_ns));
+        KI_CUDA(ctx, cudaLaunchKernelEx(&cfg, gemm_e4m3_pair_kernel, tA, tB, tC, M, N, K, alpha, ctx->d_status,
+                                        ctx->wait_timeout_ns));
         return ki::check_launch(ctx, "gemm_e4m3_pair_kernel launch");
     }
     KI_CUDA(ctx, cudaFuncSetAttribute(gemm_e4m3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));

@@ -109,6 +109,15 @@ int ki_reduce_sum_f32(ki_ctx* ctx, const float* d_x, size_t n, float* d_out_f32,
                       void* stream);
 /* sum of Int64 with two's-complement wrap-around (the shard total of the sharded scan). */
 int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out, void* stream);
+/* Device-wide reduce for any of the reference's fold operators that Base names (@warpfold takes any
+ * op, src/warp.jl:273-282; the device-wide result is Base.sum / maximum / minimum).
+ * op: KI_OP_ADD, KI_OP_MAX or KI_OP_MIN; dtype: KI_I32, KI_U32, KI_I64, KI_U64, KI_F32, KI_F64.
+ * d_out receives one value of the result type: for KI_OP_ADD Int32 -> Int64 and UInt32 -> UInt64
+ * (Base.add_sum widens), Int64/UInt64 wrap, Float32 stays Float32 (accumulated in Float64),
+ * Float64 stays Float64; for KI_OP_MAX / KI_OP_MIN the input type (NaN propagates, +0.0 > -0.0,
+ * as Base.max / Base.min).  n = 0: KI_OP_ADD writes zero, KI_OP_MAX / KI_OP_MIN return KI_ERR_ARG
+ * (Base throws on an empty maximum).  Deterministic for a given n and device. */
+int ki_reduce(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t n, void* d_out, void* stream);
 
 /* ---- (a4/a5) single-pass decoupled-lookback inclusive scan ----------------------------------
  * Replaces: @warpreduce (src/warp.jl:226-237) for the in-warp scan, @access / @fence
@@ -118,6 +127,16 @@ int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out,
  * bounded by the context's timeout. */
 int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
                           void* stream);
+/* Device-wide scan for any of those operators and types (@warpreduce takes any op,
+ * src/warp.jl:226-237; the device-wide result is Base.cumsum / accumulate(op, x; init)).
+ * op, dtype and the result type as for ki_reduce; d_out holds n values of the result type.
+ * exclusive = 0: out[i] = op(init, in[0], ..., in[i]); exclusive != 0: out[i] = op(init, in[0], ...,
+ * in[i-1]), out[0] = init.  h_init: host pointer to one value of the result type, or NULL for the
+ * operator's identity (0, the lowest value, the highest value).  in == out is allowed when the input
+ * and result types have the same size; other overlaps return KI_ERR_ARG.  Float sums accumulate in
+ * Float64 (within 1e-5*log2(n) of a Float64 scan).  Int64 + with a seed is ki_scan_inclusive_i64. */
+int ki_scan(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in, void* d_out, size_t n,
+            const void* h_init, void* stream);
 
 /* Allocation-free scan.  No counterpart in the reference.
  * For callers that cannot allocate device memory: code running while a CUDA graph is captured,

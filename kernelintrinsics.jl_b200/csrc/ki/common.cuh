@@ -23,7 +23,8 @@ enum ki_region {
     KI_REG_COMPACT = 2,
     KI_REG_MISC = 3,
     KI_REG_STAGE = 4,  // device staging slots of the host-buffer copy
-    KI_REG_COUNT = 5
+    KI_REG_SCAN_ANY = 5,  // the generic scan (any operator and type)
+    KI_REG_COUNT = 6
 };
 
 // Host-buffer copy pipeline: slots of staging memory cycled over three streams.

@@ -16,6 +16,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstring>
 
 #include "common.cuh"
 #include "intrinsics.cuh"
@@ -141,6 +142,107 @@ __device__ __forceinline__ int64_t decoupled_lookback(TileStatus st, uint64_t t,
         end -= 32 * K;
     }
     if (lane == 0) publish(st, t, kFlagPrefix, wrap_add(excl, agg));
+    return excl;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Lookback for any operator and value type of at most 8 bytes (the generic scan).  Every value
+// lives in the side arrays (aggs for aggregates, incls for inclusive prefixes, as raw bits); the
+// status word carries only the state and the wide bit.  The window logic is decoupled_lookback's;
+// once a window is usable a fence.acq_rel.gpu orders the value loads after the status loads.
+// `op` must be associative and commutative (Base + on integers, max, min; Float64 + up to rounding).
+// ---------------------------------------------------------------------------------------------
+template <class A>
+__device__ __forceinline__ uint64_t to_bits(A v) {
+    uint64_t b = 0;
+    memcpy(&b, &v, sizeof(A));
+    return b;
+}
+template <class A>
+__device__ __forceinline__ A from_bits(uint64_t b) {
+    A v;
+    memcpy(&v, &b, sizeof(A));
+    return v;
+}
+
+template <class A>
+__device__ __forceinline__ void publish_wide(TileStatus st, uint64_t t, uint64_t state, A v) {
+    uint64_t* side = reinterpret_cast<uint64_t*>(state == kFlagPrefix ? st.incls : st.aggs);
+    side[t] = to_bits(v);
+    store<Order::Release, Scope::Device>(&st.words[t], kFlagWide | state);
+}
+
+template <class A, class F>
+__device__ __forceinline__ void publish_aggregate_wide(TileStatus st, uint64_t t, A agg, A init, F op) {
+    if (t == 0) publish_wide(st, 0, kFlagPrefix, op(init, agg));
+    else publish_wide(st, t, kFlagAgg, agg);
+}
+
+// Run by all 32 lanes of one warp after publish_aggregate_wide(t).  Returns the exclusive prefix of
+// tile t (init for tile 0) and publishes tile t's inclusive prefix.
+template <int K, class A, class F>
+__device__ __forceinline__ A decoupled_lookback_wide(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
+                                                     uint32_t* status, uint64_t timeout_ns) {
+    const unsigned lane = lane0();
+    if (t == 0) return init;
+    A excl = identity;
+    long long end = (long long)t - 1;
+    uint64_t t_start = 0;
+    bool timed_out = false;
+    unsigned backoff = KI_LOOKBACK_MIN_SLEEP_NS;
+    const uint64_t* aggs = reinterpret_cast<const uint64_t*>(st.aggs);
+    const uint64_t* incls = reinterpret_cast<const uint64_t*>(st.incls);
+    while (true) {
+        uint64_t w[K];
+        int first_p, first_zero;
+        int pos_p, pos_zero;
+        while (true) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const long long idx = end - (long long)(lane * K + k);
+                w[k] = (idx >= 0) ? load<Order::Relaxed, Scope::Device>(&st.words[idx]) : (kFlagPrefix | kFlagWide);
+            }
+            first_p = K;
+            first_zero = K;
+#pragma unroll
+            for (int k = K - 1; k >= 0; --k) {
+                if ((w[k] & 3) == kFlagPrefix) first_p = k;
+                if ((w[k] & 3) == kFlagNone) first_zero = k;
+            }
+            const unsigned pm = __ballot_sync(0xffffffffu, first_p < K);
+            const unsigned zm = __ballot_sync(0xffffffffu, first_zero < K);
+            const int lp = pm ? __ffs(pm) - 1 : 32, lz = zm ? __ffs(zm) - 1 : 32;
+            pos_p = (lp < 32) ? lp * K + __shfl_sync(0xffffffffu, first_p, lp) : 32 * K;
+            pos_zero = (lz < 32) ? lz * K + __shfl_sync(0xffffffffu, first_zero, lz) : 32 * K;
+            if (pos_zero > pos_p || (pos_zero == 32 * K && pos_p == 32 * K)) break;
+            const uint64_t now = globaltimer_ns();
+            if (t_start == 0) t_start = now;
+            timed_out = __shfl_sync(0xffffffffu, (int)(now - t_start > timeout_ns), 0) != 0;
+            if (timed_out) break;
+            __nanosleep(backoff);
+            if (backoff < KI_LOOKBACK_MAX_SLEEP_NS) backoff <<= 1;
+        }
+        if (timed_out) {
+            if (lane == 0) atomicOr(status, (uint32_t)KI_DEV_TIMEOUT);
+            break;
+        }
+        fence<Scope::Device, Order::AcqRel>();
+        A v = identity;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int p = (int)lane * K + k;
+            const long long idx = end - p;
+            if (p <= pos_p && p < 32 * K && idx >= 0) {
+                const uint64_t b = ((w[k] & 3) == kFlagPrefix) ? load<Order::Relaxed, Scope::Device>(&incls[idx])
+                                                               : load<Order::Relaxed, Scope::Device>(&aggs[idx]);
+                v = op(v, from_bits<A>(b));
+            }
+        }
+        excl = op(excl, warpfold(v, op));
+        if (pos_p < 32 * K) break;
+        end -= 32 * K;
+    }
+    if (lane == 0) publish_wide(st, t, kFlagPrefix, op(excl, agg));
     return excl;
 }
 

@@ -1,4 +1,4 @@
-// reduce.cu -- grid-wide sum (Base.sum) built from @warpfold-style folds.
+// reduce.cu -- grid-wide reduce (Base.sum / maximum / minimum) built from @warpfold-style folds.
 //
 // One launch: every thread streams 16-byte vectors (several loads in flight), folds them into a
 // per-thread accumulator, the warp folds with __shfl_xor_sync (every lane holds the warp total;
@@ -7,10 +7,13 @@
 // finish (atomic ticket after a device-scope release fence) folds the partials in a fixed order and
 // writes the result, so the result is deterministic for a given n and device.
 //
-// Float32 input accumulates in Float64 once each 16-byte vector has been added in Float32, so the
-// result is within a few ulps of a Float64 sum (the parity bound is 1e-5*log2(n) relative).
+// Operators and types follow Julia Base (ki/ops.cuh): Float32 sums accumulate in Float64 once each
+// 16-byte vector has been added in Float32 (within a few ulps of a Float64 sum; the parity bound is
+// 1e-5*log2(n) relative), Int32/UInt32 sums widen to 64 bits, Int64 sums wrap, and maximum/minimum
+// propagate NaN and order signed zeros as Base.max/Base.min do.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
+#include "ki/ops.cuh"
 
 namespace {
 
@@ -28,87 +31,76 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = KI_REDUCE_UNROLL;          // 16-byte loads in flight per thread
 constexpr int kBlocksPerSm = KI_REDUCE_BLOCKS_PER_SM;
 
-template <class T>
-struct Acc;
-template <>
-struct Acc<float> {
-    using type = double;
-    __device__ static __forceinline__ double vec(const float4& v) { return (double)((v.x + v.y) + (v.z + v.w)); }
-    __device__ static __forceinline__ double one(float v) { return (double)v; }
-    __device__ static __forceinline__ double add(double a, double b) { return a + b; }
-};
-template <>
-struct Acc<int64_t> {
-    using type = int64_t;
-    __device__ static __forceinline__ int64_t vec(const longlong2& v) { return ki::wrap_add(v.x, v.y); }
-    __device__ static __forceinline__ int64_t one(int64_t v) { return v; }
-    __device__ static __forceinline__ int64_t add(int64_t a, int64_t b) { return ki::wrap_add(a, b); }
-};
-
-template <class T>
-struct Vec;
-template <>
-struct Vec<float> {
-    using type = float4;
-};
-template <>
-struct Vec<int64_t> {
-    using type = longlong2;
-};
-
-struct AddOp {
-    template <class A>
-    __device__ __forceinline__ A operator()(A a, A b) const {
-        if constexpr (std::is_same<A, int64_t>::value) return ki::wrap_add(a, b);
-        else return a + b;
+// Fold of one 16-byte vector into the accumulation type.  Float32 sums add the four lanes in
+// Float32 first (one rounding per vector), everything else folds in the accumulation type.
+template <class T, class Op>
+__device__ __forceinline__ typename ki::Traits<T, Op>::A fold_vec(const ki::Vec16<T>& v) {
+    using Tr = ki::Traits<T, Op>;
+    using A = typename Tr::A;
+    constexpr int kV = (int)(16 / sizeof(T));
+    if constexpr (std::is_same<T, float>::value && std::is_same<Op, ki::JAdd>::value) {
+        return (double)((v.v[0] + v.v[1]) + (v.v[2] + v.v[3]));
+    } else {
+        A r = (A)v.v[0];
+#pragma unroll
+        for (int i = 1; i < kV; ++i) r = Tr::op(r, (A)v.v[i]);
+        return r;
     }
-};
+}
 
-template <class A>
-__device__ __forceinline__ A block_fold(A v, A* sm) {
+template <class A, class F>
+__device__ __forceinline__ A block_fold(A v, A* sm, F f, A id) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    v = ki::warpfold(v, AddOp{});
+    v = ki::warpfold(v, f);
     if (lane == 0) sm[w] = v;
     __syncthreads();
-    A r = A(0);
+    A r = id;
     if (w == 0) {
-        r = (lane < kWarps) ? sm[lane] : A(0);
-        r = ki::warpfold(r, AddOp{});
+        r = (lane < kWarps) ? sm[lane] : id;
+        r = ki::warpfold(r, f);
     }
     return r;  // valid in warp 0
 }
 
-template <class T>
-__global__ void __launch_bounds__(kThreads) reduce_kernel(const T* __restrict__ x, size_t head, size_t nvec,
-                                                          size_t n, typename Acc<T>::type* partials,
-                                                          unsigned int* ticket, float* out_f32,
-                                                          typename Acc<T>::type* out_acc) {
-    using A = typename Acc<T>::type;
-    using V = typename Vec<T>::type;
+template <class T, class Op>
+__global__ void __launch_bounds__(kThreads)
+    reduce_kernel(const T* __restrict__ x, size_t head, size_t nvec, size_t n, typename ki::Traits<T, Op>::A* partials,
+                  unsigned int* ticket, typename ki::Traits<T, Op>::R* out, typename ki::Traits<T, Op>::A* out_acc) {
+    using Tr = ki::Traits<T, Op>;
+    using A = typename Tr::A;
+    using V = ki::Vec16<T>;
     constexpr int kVec = (int)(16 / sizeof(T));
+    const ki::OpFn<T, Op> f;
+    const A id = Tr::identity();
     __shared__ A sm[kWarps];
     __shared__ int is_last;
 
     const V* xv = reinterpret_cast<const V*>(x + head);
     const size_t stride = (size_t)gridDim.x * kThreads;
     size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x;
-    A acc = A(0);
+    A acc = id;
     for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
         V v[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) v[u] = __ldcs(xv + i + u * stride);
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(xv + i + u * stride));
+            v[u] = *reinterpret_cast<const V*>(&raw);
+        }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) acc = Acc<T>::add(acc, Acc<T>::vec(v[u]));
+        for (int u = 0; u < kUnroll; ++u) acc = Tr::op(acc, fold_vec<T, Op>(v[u]));
     }
-    for (; i < nvec; i += stride) acc = Acc<T>::add(acc, Acc<T>::vec(__ldcs(xv + i)));
+    for (; i < nvec; i += stride) {
+        const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(xv + i));
+        acc = Tr::op(acc, fold_vec<T, Op>(*reinterpret_cast<const V*>(&raw)));
+    }
     // unaligned head and the tail that does not fill a vector
     if (blockIdx.x == 0) {
         const size_t tail0 = head + nvec * kVec;
         const int t = threadIdx.x;
-        if ((size_t)t < head) acc = Acc<T>::add(acc, Acc<T>::one(x[t]));
-        if ((size_t)t < n - tail0) acc = Acc<T>::add(acc, Acc<T>::one(x[tail0 + t]));
+        if ((size_t)t < head) acc = Tr::op(acc, (A)x[t]);
+        if ((size_t)t < n - tail0) acc = Tr::op(acc, (A)x[tail0 + t]);
     }
-    A bsum = block_fold(acc, sm);
+    A bsum = block_fold(acc, sm, f, id);
     if (threadIdx.x == 0) {
         partials[blockIdx.x] = bsum;
         ki::fence<ki::Scope::Device, ki::Order::AcqRel>();
@@ -118,22 +110,22 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(const T* __restrict__ 
     __syncthreads();
     if (!is_last) return;
     ki::fence<ki::Scope::Device, ki::Order::AcqRel>();
-    A r = A(0);
+    A r = id;
     for (unsigned b = threadIdx.x; b < gridDim.x; b += kThreads)
-        r = Acc<T>::add(r, ki::load<ki::Order::Relaxed, ki::Scope::Device>(partials + b));
+        r = Tr::op(r, ki::load<ki::Order::Relaxed, ki::Scope::Device>(partials + b));
     __syncthreads();  // sm reuse
-    r = block_fold(r, sm);
+    r = block_fold(r, sm, f, id);
     if (threadIdx.x == 0) {
         if (out_acc) *out_acc = r;
-        if (out_f32) *out_f32 = (float)r;
+        if (out) *out = (typename Tr::R)r;
         *ticket = 0u;  // ready for the next call on this stream
     }
 }
 
-template <class T>
-int launch_reduce(ki_ctx* ctx, const T* x, size_t n, float* out_f32, typename Acc<T>::type* out_acc,
-                  cudaStream_t s) {
-    using A = typename Acc<T>::type;
+template <class T, class Op>
+int launch_reduce(ki_ctx* ctx, const T* x, size_t n, typename ki::Traits<T, Op>::R* out,
+                  typename ki::Traits<T, Op>::A* out_acc, cudaStream_t s) {
+    using A = typename ki::Traits<T, Op>::A;
     constexpr int kVec = (int)(16 / sizeof(T));
     size_t head = (size_t)((16 - (reinterpret_cast<uintptr_t>(x) & 15)) & 15) / sizeof(T);
     if (head > n) head = n;
@@ -148,8 +140,37 @@ int launch_reduce(ki_ctx* ctx, const T* x, size_t n, float* out_f32, typename Ac
     if (rc) return rc;
     unsigned int* ticket = reinterpret_cast<unsigned int*>(base);
     A* partials = reinterpret_cast<A*>(static_cast<char*>(base) + 256);
-    reduce_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(x, head, nvec, n, partials, ticket, out_f32, out_acc);
+    reduce_kernel<T, Op><<<(unsigned)blocks, kThreads, 0, s>>>(x, head, nvec, n, partials, ticket, out, out_acc);
     return ki::check_launch(ctx, "reduce_kernel launch");
+}
+
+template <class T, class Op>
+int reduce_generic(ki_ctx* ctx, const void* d_x, size_t n, void* d_out, cudaStream_t s) {
+    using R = typename ki::Traits<T, Op>::R;
+    if (n > 0 && !ki::aligned(d_x, sizeof(T))) return ki::set_error(ctx, KI_ERR_ARG, "reduce: misaligned input");
+    if (!ki::aligned(d_out, sizeof(R))) return ki::set_error(ctx, KI_ERR_ARG, "reduce: misaligned output");
+    if (n == 0) {
+        if constexpr (!std::is_same<Op, ki::JAdd>::value) {
+            return ki::set_error(ctx, KI_ERR_ARG, "reduce: maximum/minimum over an empty collection");
+        } else {
+            KI_CUDA(ctx, cudaMemsetAsync(d_out, 0, sizeof(R), s));
+            return KI_OK;
+        }
+    }
+    return launch_reduce<T, Op>(ctx, static_cast<const T*>(d_x), n, static_cast<R*>(d_out), nullptr, s);
+}
+
+template <class Op>
+int reduce_dtype(ki_ctx* ctx, int dtype, const void* d_x, size_t n, void* d_out, cudaStream_t s) {
+    switch (dtype) {
+        case KI_I32: return reduce_generic<int32_t, Op>(ctx, d_x, n, d_out, s);
+        case KI_U32: return reduce_generic<uint32_t, Op>(ctx, d_x, n, d_out, s);
+        case KI_I64: return reduce_generic<int64_t, Op>(ctx, d_x, n, d_out, s);
+        case KI_U64: return reduce_generic<uint64_t, Op>(ctx, d_x, n, d_out, s);
+        case KI_F32: return reduce_generic<float, Op>(ctx, d_x, n, d_out, s);
+        case KI_F64: return reduce_generic<double, Op>(ctx, d_x, n, d_out, s);
+        default: return ki::set_error(ctx, KI_ERR_ARG, "reduce: dtype must be Int32/UInt32/Int64/UInt64/Float32/Float64");
+    }
 }
 
 }  // namespace
@@ -167,7 +188,7 @@ extern "C" int ki_reduce_sum_f32(ki_ctx* ctx, const float* d_x, size_t n, float*
         if (d_out_f64) KI_CUDA(ctx, cudaMemsetAsync(d_out_f64, 0, sizeof(double), s));
         return KI_OK;
     }
-    return launch_reduce<float>(ctx, d_x, n, d_out_f32, d_out_f64, s);
+    return launch_reduce<float, ki::JAdd>(ctx, d_x, n, d_out_f32, d_out_f64, s);
 }
 
 extern "C" int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out, void* stream) {
@@ -181,5 +202,19 @@ extern "C" int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int6
         KI_CUDA(ctx, cudaMemsetAsync(d_out, 0, sizeof(int64_t), s));
         return KI_OK;
     }
-    return launch_reduce<int64_t>(ctx, d_x, n, nullptr, d_out, s);
+    return launch_reduce<int64_t, ki::JAdd>(ctx, d_x, n, d_out, nullptr, s);
+}
+
+extern "C" int ki_reduce(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t n, void* d_out, void* stream) {
+    KI_CHECK_CTX(ctx);
+    if (!d_out) return ki::set_error(ctx, KI_ERR_ARG, "reduce: no output");
+    if (n > 0 && !d_x) return ki::set_error(ctx, KI_ERR_ARG, "reduce: null input");
+    KI_GUARD(ctx);
+    cudaStream_t s = ki::as_stream(stream);
+    switch (op) {
+        case KI_OP_ADD: return reduce_dtype<ki::JAdd>(ctx, dtype, d_x, n, d_out, s);
+        case KI_OP_MAX: return reduce_dtype<ki::JMax>(ctx, dtype, d_x, n, d_out, s);
+        case KI_OP_MIN: return reduce_dtype<ki::JMin>(ctx, dtype, d_x, n, d_out, s);
+        default: return ki::set_error(ctx, KI_ERR_ARG, "reduce: op must be KI_OP_ADD, KI_OP_MAX or KI_OP_MIN");
+    }
 }

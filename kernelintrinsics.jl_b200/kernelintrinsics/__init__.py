@@ -30,7 +30,7 @@ __all__ = [
     "Up", "Down", "Xor", "Idx", "All", "AnyLane", "Uni", "Ballot", "KIError", "KIArgumentError",
     "KITimeoutError", "Context", "context", "warpsize", "get_warpsize", "devices", "shfl", "warpreduce",
     "warpfold", "vote", "vload", "vstore", "vload_multi", "vstore_multi", "generate_partN", "access",
-    "message_pass", "vcopy", "vcopy_host", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
+    "message_pass", "vcopy", "vcopy_host", "reduce", "scan", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
     "fp8_gemm", "fill_uniform", "fill_int_range", "fill_bytes", "fill_normal", "fill_e4m3_uniform",
 ]
 
@@ -472,6 +472,54 @@ def warpreduce_scan(x, out=None, seed: int = 0, stream=None):
     out = torch.empty_like(x) if out is None else out
     context(d).call("ki_scan_inclusive_i64", _ptr(x), _ptr(out), x.numel(), ctypes.c_int64(int(seed)),
                     _stream_ptr(stream, d))
+    return out
+
+
+# Result dtype of Base.sum / cumsum (add_sum widens small integers) and of maximum/minimum (same type).
+def _result_dtype(dtype, op: str):
+    torch = _torch()
+    if op in ("+", "add") and dtype in (torch.int32, torch.uint32):
+        return torch.int64 if dtype == torch.int32 else torch.uint64
+    return dtype
+
+
+_GENERIC_OPS = {"+": 0, "add": 0, "max": 1, "min": 2}
+
+
+def reduce(x, op: str = "+", out=None, stream=None):
+    """sum / maximum / minimum of Int32, UInt32, Int64, UInt64, Float32 or Float64 ``x`` with Julia Base
+    semantics (the device-wide @warpfold): Int32/UInt32 sums widen to 64 bits, Float32 sums
+    accumulate in Float64, maximum/minimum propagate NaN.  Returns a device scalar."""
+    torch = _torch()
+    d = _dev(x)
+    if op not in _GENERIC_OPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"reduce: op must be one of {sorted(_GENERIC_OPS)}")
+    x = x.contiguous()
+    out = torch.empty((), dtype=_result_dtype(x.dtype, op), device=x.device) if out is None else out
+    context(d).call("ki_reduce", _GENERIC_OPS[op], _dtype_code(x), _ptr(x), x.numel(), _ptr(out),
+                    _stream_ptr(stream, d))
+    return out
+
+
+def scan(x, op: str = "+", exclusive: bool = False, init=None, out=None, stream=None):
+    """accumulate(op, x; init) / cumsum for Int32, UInt32, Int64, UInt64, Float32 or Float64 ``x``
+    (the device-wide @warpreduce).  The result has Base's type (widened for Int32/UInt32 sums);
+    ``exclusive`` shifts it by one element and starts at ``init`` (the identity when None)."""
+    import numpy as np
+
+    torch = _torch()
+    d = _dev(x)
+    if op not in _GENERIC_OPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"scan: op must be one of {sorted(_GENERIC_OPS)}")
+    rd = _result_dtype(x.dtype, op)
+    out = torch.empty(x.shape, dtype=rd, device=x.device) if out is None else out
+    init_buf = None
+    if init is not None:
+        np_dt = {torch.int32: np.int32, torch.uint32: np.uint32, torch.int64: np.int64, torch.uint64: np.uint64,
+                 torch.float32: np.float32, torch.float64: np.float64}[rd]
+        init_buf = np.array([init], dtype=np_dt)
+    context(d).call("ki_scan", _GENERIC_OPS[op], _dtype_code(x), int(bool(exclusive)), _ptr(x), _ptr(out), x.numel(),
+                    ctypes.c_void_p(init_buf.ctypes.data) if init_buf is not None else None, _stream_ptr(stream, d))
     return out
 
 

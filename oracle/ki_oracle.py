@@ -18,6 +18,10 @@ Two layers:
   - ``vote``           ext/CUDA/shuffle_vote.jl:23-34 (vote.sync semantics; ballot is UInt32)
   - ``generate_partN`` src/vectorization.jl:306-338
   - ``vload_multi``    src/vectorization.jl:365-379 (mod selects the piece pattern)
+
+* numpy restatements of the device-wide reduce and scan for +, max and min (``accumulate``,
+  ``reduce_op``) with Julia Base semantics: widening small-integer sums, wrapping Int64 sums,
+  NaN-propagating max/min with -0.0 < +0.0.
 """
 from __future__ import annotations
 
@@ -175,6 +179,88 @@ def cumsum_i64(x: np.ndarray, seed: int = 0, nthreads: int = 0) -> np.ndarray:
     y = np.empty_like(x)
     lib().ko_cumsum_i64(_ptr(x), _ptr(y), x.size, seed, nthreads)
     return y
+
+
+# ---------------------------------------------------------------------------------------------
+# Device-wide reduce / scan for +, max, min (the device-wide uses of @warpfold and @warpreduce,
+# src/warp.jl:273-282 and :226-237, which take any operator): Julia Base semantics of
+# sum / maximum / minimum and cumsum / accumulate(op, x; init).
+#   * +    Int32 -> Int64 and UInt32 -> UInt64 (Base.add_sum widens), Int64/UInt64 wrap,
+#          floats in Float64 (the device's Float32 result is compared within a tolerance);
+#   * max  NaN wins, +0.0 > -0.0 (Base.max); min: NaN wins, -0.0 < +0.0 (Base.min).
+# ---------------------------------------------------------------------------------------------
+def result_dtype(dtype, op: str):
+    dtype = np.dtype(dtype)
+    if op == "+" and dtype == np.int32:
+        return np.dtype(np.int64)
+    if op == "+" and dtype == np.uint32:
+        return np.dtype(np.uint64)
+    if op == "+" and dtype.kind == "f":
+        return np.dtype(np.float64)
+    return dtype
+
+
+def _float_keys(x: np.ndarray, op: str) -> np.ndarray:
+    """Unsigned keys whose order is Base.isless with -0.0 < +0.0; NaN maps to the winning end."""
+    bits_t = np.uint32 if x.dtype == np.float32 else np.uint64
+    top = bits_t(1) << bits_t(8 * x.dtype.itemsize - 1)
+    b = x.view(bits_t)
+    k = np.where(b & top, ~b, b | top).astype(bits_t)
+    nan = np.isnan(x)
+    return np.where(nan, np.iinfo(bits_t).max if op == "max" else 0, k).astype(bits_t)
+
+
+def _from_keys(k: np.ndarray, dtype, op: str) -> np.ndarray:
+    bits_t = np.uint32 if np.dtype(dtype) == np.float32 else np.uint64
+    top = bits_t(1) << bits_t(8 * np.dtype(dtype).itemsize - 1)
+    nan_key = np.iinfo(bits_t).max if op == "max" else 0
+    b = np.where(k & top, k & ~top, ~k).astype(bits_t)
+    v = b.view(dtype).copy()
+    v[k == nan_key] = np.nan
+    return v
+
+
+def accumulate(op: str, x: np.ndarray, init=None, exclusive: bool = False) -> np.ndarray:
+    """accumulate(op, x; init) with Base semantics; exclusive shifts by one and starts at init."""
+    x = np.ascontiguousarray(x)
+    rd = result_dtype(x.dtype, op)
+    if op == "+":
+        v = np.cumsum(x.astype(rd), dtype=rd)  # numpy wraps integer overflow like Base
+        if init is not None:
+            v = (v + rd.type(init)).astype(rd) if rd.kind != "f" else v + float(init)
+    elif x.dtype.kind == "f":
+        keys = _float_keys(x, op)
+        if init is not None:
+            keys = np.concatenate([_float_keys(np.array([init], dtype=x.dtype), op), keys])
+        acc = (np.maximum if op == "max" else np.minimum).accumulate(keys)
+        if init is not None:
+            acc = acc[1:]
+        v = _from_keys(acc, x.dtype, op)
+    else:
+        seq = x if init is None else np.concatenate([np.array([init], dtype=x.dtype), x])
+        v = (np.maximum if op == "max" else np.minimum).accumulate(seq)
+        if init is not None:
+            v = v[1:]
+    if not exclusive:
+        return v
+    if init is None:
+        if op == "+":
+            init = 0
+        elif rd.kind == "f":
+            init = -np.inf if op == "max" else np.inf
+        else:
+            init = np.iinfo(rd).min if op == "max" else np.iinfo(rd).max
+    return np.concatenate([np.array([init], dtype=rd), v[:-1]])
+
+
+def reduce_op(op: str, x: np.ndarray):
+    """sum / maximum / minimum with Base semantics (raises on an empty maximum / minimum)."""
+    x = np.ascontiguousarray(x)
+    if x.size == 0:
+        if op == "+":
+            return result_dtype(x.dtype, op).type(0)
+        raise ValueError("reducing over an empty collection is not allowed")
+    return accumulate(op, x)[-1]
 
 
 def filter_gt_f32(x: np.ndarray, thr: float, index_base: int = 1, nthreads: int = 0):

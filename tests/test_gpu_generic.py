@@ -1,0 +1,151 @@
+"""GPU: device-wide reduce and scan for +, max, min over Int32/UInt32/Int64/UInt64/Float32/Float64
+(ki_reduce, ki_scan) against the oracle's Julia Base semantics.
+
+Integers are bit-exact.  Float sums: |device - Float64 oracle| <= 1e-5*log2(n) * (running sum of |x|),
+the tolerance the workload definition states for Float32 reduce/scan.  max/min are exact, NaN included.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+NP_TYPES = [np.int32, np.uint32, np.int64, np.uint64, np.float32, np.float64]
+OPS = ["+", "max", "min"]
+
+
+def _data(dt, n, seed, op="max"):
+    rng = np.random.default_rng(seed)
+    dt = np.dtype(dt)
+    if dt.kind == "f":
+        x = rng.standard_normal(n).astype(dt)
+        if n > 10 and op != "+":  # for max/min: signed zeros, infinities (NaN has its own test)
+            x[rng.integers(0, n, 3)] = -0.0
+            x[rng.integers(0, n, 3)] = 0.0
+            x[rng.integers(0, n, 1)] = np.inf if seed % 2 else -np.inf
+        return x
+    if dt.kind == "u":
+        return rng.integers(0, np.iinfo(dt).max, n, dtype=dt, endpoint=True)
+    return rng.integers(np.iinfo(dt).min, np.iinfo(dt).max, n, dtype=dt, endpoint=True)
+
+
+def _to_dev(x, dev):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def _check(got, want, x, op):
+    if np.dtype(want.dtype).kind == "f" and op == "+":
+        n = max(2, x.size)
+        scale = np.cumsum(np.abs(x.astype(np.float64)))
+        err = np.abs(got.astype(np.float64) - want)
+        assert (err <= 1e-5 * math.log2(n) * np.maximum(scale, 1e-30)).all(), float((err / np.maximum(scale, 1e-30)).max())
+    elif np.dtype(want.dtype).kind == "f":
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        m = ~np.isnan(want)
+        assert np.array_equal(got[m].view(np.uint8), want[m].astype(got.dtype).view(np.uint8))  # signed zeros too
+    else:
+        assert np.array_equal(got, want)
+
+
+SIZES = [1, 2, 31, 33, 1000, 15871, 15872, 15873, 31743, 31744, 31745, 100_003, (1 << 20) + 3]
+
+
+@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("op", OPS)
+def test_scan_inclusive_and_exclusive(KI, oracle, dev, dt, op):
+    for k, n in enumerate(SIZES):
+        x = _data(dt, n, 10 * k + 1, op)
+        xd = _to_dev(x, dev)
+        for excl in (False, True):
+            got = KI.scan(xd, op, exclusive=excl).cpu().numpy()
+            want = oracle.accumulate(op, x, exclusive=excl)
+            _check(got, want, x if not excl else np.concatenate([[0], x[:-1]]).astype(x.dtype), op)
+    KI.context(0).check()
+
+
+@pytest.mark.parametrize("dt", [np.int32, np.int64, np.float32, np.float64], ids=lambda d: np.dtype(d).name)
+def test_scan_init_misaligned_and_in_place(KI, oracle, dev, dt):
+    import torch
+
+    n = 3 * 31744 + 11
+    x = _data(dt, n + 1, 7, "+")
+    base = _to_dev(x, dev)
+    xs = base[1:]  # 4- or 8-byte offset: the plain-load path
+    init = 5 if np.dtype(dt).kind != "f" else 0.25
+    for op in OPS:
+        got = KI.scan(xs, op, init=init).cpu().numpy()
+        want = oracle.accumulate(op, x[1:], init=init)
+        _check(got, want, x[1:], op)
+    if np.dtype(dt).itemsize == 8:  # result type as wide as the input: in place
+        y = xs.clone()
+        KI.scan(y, "max", out=y)
+        assert np.array_equal(y.cpu().numpy(), oracle.accumulate("max", x[1:]))
+    elif np.dtype(dt).kind == "i":  # a widened result cannot alias its input
+        wide = torch.empty(n, dtype=torch.int64, device=dev)
+        narrow = wide.view(torch.int32)[:n]
+        with pytest.raises(KI.KIArgumentError):
+            KI.scan(narrow, "+", out=wide)
+    KI.context(0).check()
+
+
+def test_scan_nan_and_extremes(KI, oracle, dev):
+    x = np.array([1.0, np.nan, -np.inf, 2.0, -0.0, 0.0] * 7000, dtype=np.float32)
+    xd = _to_dev(x, dev)
+    for op in ("max", "min"):
+        got = KI.scan(xd, op).cpu().numpy()
+        _check(got, oracle.accumulate(op, x), x, op)
+    # Int64 wrap-around and Int32 widening
+    big = np.full(40000, np.iinfo(np.int64).max // 3, dtype=np.int64)
+    assert np.array_equal(KI.scan(_to_dev(big, dev), "+").cpu().numpy(), oracle.accumulate("+", big))
+    i32 = np.full(40000, np.iinfo(np.int32).max, dtype=np.int32)
+    got = KI.scan(_to_dev(i32, dev), "+").cpu().numpy()
+    assert got.dtype == np.int64 and np.array_equal(got, oracle.accumulate("+", i32))
+
+
+@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("op", OPS)
+def test_reduce(KI, oracle, dev, dt, op):
+    for k, n in enumerate([1, 7, 33, 4099, 1 << 16, (1 << 22) + 5]):
+        x = _data(dt, n, 100 + k, op)
+        got = KI.reduce(_to_dev(x, dev), op).cpu().numpy().reshape(1)
+        want = np.array([oracle.reduce_op(op, x)])
+        if np.dtype(dt).kind == "f" and op == "+":
+            assert abs(float(got[0]) - float(want[0])) <= 1e-5 * math.log2(max(2, n)) * float(np.abs(x.astype(np.float64)).sum())
+        else:
+            _check(got, want.astype(got.dtype), x, op)
+    KI.context(0).check()
+
+
+def test_reduce_empty_and_nan(KI, dev):
+    import torch
+
+    e = torch.empty(0, dtype=torch.float32, device=dev)
+    assert KI.reduce(e, "+").item() == 0.0
+    with pytest.raises(KI.KIArgumentError):
+        KI.reduce(e, "max")
+    x = torch.tensor([1.0, float("nan"), 3.0] * 5000, dtype=torch.float64, device=dev)
+    assert math.isnan(KI.reduce(x, "max").item()) and math.isnan(KI.reduce(x, "min").item())
+    z = torch.tensor([-0.0, 0.0, -0.0], dtype=torch.float32, device=dev)
+    assert math.copysign(1.0, KI.reduce(z, "max").item()) == 1.0
+    assert math.copysign(1.0, KI.reduce(z, "min").item()) == -1.0
+
+
+def test_scan_config_size_f32(KI, dev):
+    """Float32 cumsum at n = 2^28 (uniform[0,1) from the device generator): within 1e-5*log2(n) of a
+    Float64 scan, checked on the device in Float64."""
+    import torch
+
+    n = 1 << 28
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    KI.fill_uniform(x, seed=1)
+    y = KI.scan(x, "+")
+    ref = torch.cumsum(x.double(), 0)
+    rel = ((y.double() - ref).abs() / ref.clamp_min(1e-30)).max().item()
+    assert rel <= 1e-5 * 28, rel
+    del x, y, ref
+    torch.cuda.empty_cache()

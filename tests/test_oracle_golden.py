@@ -139,3 +139,44 @@ def test_copy_and_gemm_oracle(oracle):
     got = oracle.gemm_e4m3_rows(A, B, 0, 64)
     assert np.allclose(got, ref, rtol=0, atol=1e-9)
     assert np.allclose(oracle.gemm_e4m3_rows(A, B, 10, 20, scale=0.5), 0.5 * ref[10:20])
+
+
+def test_accumulate_matches_scalar_base_semantics(oracle):
+    """The vectorised Base restatement against a scalar loop of Base.max / Base.min / + on special values."""
+    import math
+
+    def jmax(a, b):
+        if math.isnan(a):
+            return a
+        if math.isnan(b):
+            return b
+        if a == b:
+            return b if math.copysign(1.0, a) < 0 else a
+        return a if a > b else b
+
+    def jmin(a, b):
+        if math.isnan(a):
+            return a
+        if math.isnan(b):
+            return b
+        if a == b:
+            return a if math.copysign(1.0, a) < 0 else b
+        return a if a < b else b
+
+    rng = np.random.default_rng(5)
+    pool = np.array([0.0, -0.0, 1.5, -2.0, np.inf, -np.inf, np.nan, 3.25], dtype=np.float64)
+    for dt in (np.float32, np.float64):
+        x = pool[rng.integers(0, pool.size, 200)].astype(dt)
+        for op, f in (("max", jmax), ("min", jmin)):
+            got = oracle.accumulate(op, x)
+            acc = float(x[0])
+            for i in range(x.size):
+                acc = float(x[0]) if i == 0 else f(acc, float(x[i]))
+                g = float(got[i])
+                assert (math.isnan(g) and math.isnan(acc)) or (g == acc and math.copysign(1, g) == math.copysign(1, acc))
+    i32 = np.array([2**31 - 1, 2**31 - 1, -5], dtype=np.int32)
+    assert oracle.accumulate("+", i32).tolist() == [2**31 - 1, 2**32 - 2, 2**32 - 7]
+    i64 = np.array([2**63 - 1, 1], dtype=np.int64)
+    assert oracle.accumulate("+", i64).tolist() == [2**63 - 1, -2**63]
+    assert oracle.accumulate("+", np.array([1, 2, 3], dtype=np.int64), init=10, exclusive=True).tolist() == [10, 11, 13]
+    assert oracle.reduce_op("+", np.zeros(0, dtype=np.int32)) == 0

@@ -146,11 +146,13 @@ __device__ __forceinline__ int64_t decoupled_lookback(TileStatus st, uint64_t t,
 }
 
 // ---------------------------------------------------------------------------------------------
-// Lookback for any operator and value type of at most 8 bytes (the generic scan).  Every value
-// lives in the side arrays (aggs for aggregates, incls for inclusive prefixes, as raw bits); the
-// status word carries only the state and the wide bit.  The window logic is decoupled_lookback's;
-// once a window is usable a fence.acq_rel.gpu orders the value loads after the status loads.
-// `op` must be associative and commutative (Base + on integers, max, min; Float64 + up to rounding).
+// Lookback for any operator and value type of at most 8 bytes (the generic scan).  A value rides in
+// its status word when it fits, as in decoupled_lookback: 4-byte values always (bits 32-63),
+// 8-byte integers when their two's-complement value fits 61 bits (bits 3-63).  Anything else
+// (every Float64, large 64-bit integers) lives in the side arrays (aggs for aggregates, incls for
+// inclusive prefixes, as raw bits) with the wide bit set in its status word; a fence.acq_rel.gpu
+// orders those value loads after the status loads.  `op` must be associative and commutative
+// (Base + on integers, max, min; Float64 + up to rounding).
 // ---------------------------------------------------------------------------------------------
 template <class A>
 __device__ __forceinline__ uint64_t to_bits(A v) {
@@ -165,24 +167,50 @@ __device__ __forceinline__ A from_bits(uint64_t b) {
     return v;
 }
 
+// Packing of a value into a status word (state in bits 0-1, wide bit 2).
 template <class A>
-__device__ __forceinline__ void publish_wide(TileStatus st, uint64_t t, uint64_t state, A v) {
-    uint64_t* side = reinterpret_cast<uint64_t*>(state == kFlagPrefix ? st.incls : st.aggs);
-    side[t] = to_bits(v);
-    store<Order::Release, Scope::Device>(&st.words[t], kFlagWide | state);
+__device__ __forceinline__ bool pack_value(A v, uint64_t& word_bits) {
+    if constexpr (sizeof(A) == 4) {
+        word_bits = to_bits(v) << 32;
+        return true;
+    } else if constexpr (std::is_integral<A>::value) {
+        const int64_t s = (int64_t)to_bits(v);
+        if (!fits61(s)) return false;
+        word_bits = (uint64_t)s << 3;
+        return true;
+    } else {
+        return false;
+    }
+}
+template <class A>
+__device__ __forceinline__ A unpack_value(uint64_t w) {
+    if constexpr (sizeof(A) == 4) return from_bits<A>(w >> 32);
+    else return from_bits<A>((uint64_t)((int64_t)w >> 3));
+}
+
+template <class A>
+__device__ __forceinline__ void publish_any(TileStatus st, uint64_t t, uint64_t state, A v) {
+    uint64_t packed;
+    if (pack_value(v, packed)) {
+        store<Order::Release, Scope::Device>(&st.words[t], packed | state);
+    } else {
+        uint64_t* side = reinterpret_cast<uint64_t*>(state == kFlagPrefix ? st.incls : st.aggs);
+        side[t] = to_bits(v);
+        store<Order::Release, Scope::Device>(&st.words[t], kFlagWide | state);
+    }
 }
 
 template <class A, class F>
-__device__ __forceinline__ void publish_aggregate_wide(TileStatus st, uint64_t t, A agg, A init, F op) {
-    if (t == 0) publish_wide(st, 0, kFlagPrefix, op(init, agg));
-    else publish_wide(st, t, kFlagAgg, agg);
+__device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op) {
+    if (t == 0) publish_any(st, 0, kFlagPrefix, op(init, agg));
+    else publish_any(st, t, kFlagAgg, agg);
 }
 
-// Run by all 32 lanes of one warp after publish_aggregate_wide(t).  Returns the exclusive prefix of
+// Run by all 32 lanes of one warp after publish_aggregate_any(t).  Returns the exclusive prefix of
 // tile t (init for tile 0) and publishes tile t's inclusive prefix.
 template <int K, class A, class F>
-__device__ __forceinline__ A decoupled_lookback_wide(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
-                                                     uint32_t* status, uint64_t timeout_ns) {
+__device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
+                                                    uint32_t* status, uint64_t timeout_ns) {
     const unsigned lane = lane0();
     if (t == 0) return init;
     A excl = identity;
@@ -200,7 +228,7 @@ __device__ __forceinline__ A decoupled_lookback_wide(TileStatus st, uint64_t t, 
 #pragma unroll
             for (int k = 0; k < K; ++k) {
                 const long long idx = end - (long long)(lane * K + k);
-                w[k] = (idx >= 0) ? load<Order::Relaxed, Scope::Device>(&st.words[idx]) : (kFlagPrefix | kFlagWide);
+                w[k] = (idx >= 0) ? load<Order::Relaxed, Scope::Device>(&st.words[idx]) : kFlagPrefix;
             }
             first_p = K;
             first_zero = K;
@@ -226,23 +254,35 @@ __device__ __forceinline__ A decoupled_lookback_wide(TileStatus st, uint64_t t, 
             if (lane == 0) atomicOr(status, (uint32_t)KI_DEV_TIMEOUT);
             break;
         }
-        fence<Scope::Device, Order::AcqRel>();
+        // values of the words at positions <= pos_p (all of the window when it holds no P)
+        bool any_wide = false;
         A v = identity;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
             const int p = (int)lane * K + k;
-            const long long idx = end - p;
-            if (p <= pos_p && p < 32 * K && idx >= 0) {
-                const uint64_t b = ((w[k] & 3) == kFlagPrefix) ? load<Order::Relaxed, Scope::Device>(&incls[idx])
-                                                               : load<Order::Relaxed, Scope::Device>(&aggs[idx]);
-                v = op(v, from_bits<A>(b));
+            if (p <= pos_p && p < 32 * K && end - p >= 0) {
+                if (w[k] & kFlagWide) any_wide = true;
+                else v = op(v, unpack_value<A>(w[k]));
+            }
+        }
+        if (__any_sync(0xffffffffu, any_wide)) {
+            fence<Scope::Device, Order::AcqRel>();
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int p = (int)lane * K + k;
+                const long long idx = end - p;
+                if (p <= pos_p && p < 32 * K && idx >= 0 && (w[k] & kFlagWide)) {
+                    const uint64_t b = ((w[k] & 3) == kFlagPrefix) ? load<Order::Relaxed, Scope::Device>(&incls[idx])
+                                                                   : load<Order::Relaxed, Scope::Device>(&aggs[idx]);
+                    v = op(v, from_bits<A>(b));
+                }
             }
         }
         excl = op(excl, warpfold(v, op));
         if (pos_p < 32 * K) break;
         end -= 32 * K;
     }
-    if (lane == 0) publish_wide(st, t, kFlagPrefix, op(excl, agg));
+    if (lane == 0) publish_any(st, t, kFlagPrefix, op(excl, agg));
     return excl;
 }
 

@@ -6,10 +6,13 @@
 //   Max  maximum / accumulate(max): a NaN operand wins, +0.0 is larger than -0.0 (Base.max).
 //   Min  minimum / accumulate(min): a NaN operand wins, -0.0 is smaller than +0.0 (Base.min).
 //
-// Traits<T, Op> gives the accumulation type A, the result type R and the identity of A.
+// Traits<T, Op> gives the accumulation type A, the result type R, lift (T -> A), lower (A -> R),
+// the identity of A and the operator on A.
 #pragma once
 
+#include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <type_traits>
 
 namespace ki {
@@ -28,24 +31,30 @@ __device__ __forceinline__ T jadd(T a, T b) {
     }
 }
 
+// Base.max / Base.min for floats, as selects (no branches): a NaN operand wins and the sign bit
+// orders equal zeros.
 template <class T>
-__device__ __forceinline__ T jmax(T a, T b) {
+__device__ __forceinline__ T jmax(T x, T y) {
     if constexpr (std::is_floating_point<T>::value) {
-        if (a != a) return a;
-        if (b != b) return b;
-        if (a == b) return signbit(a) ? b : a;  // +0.0 over -0.0
+        const bool take_y = (y > x) | (signbit(y) < signbit(x));
+        const T yy = (x != x) ? x : y;
+        const T xx = (y != y) ? y : x;
+        return take_y ? yy : xx;
+    } else {
+        return x > y ? x : y;
     }
-    return a > b ? a : b;
 }
 
 template <class T>
-__device__ __forceinline__ T jmin(T a, T b) {
+__device__ __forceinline__ T jmin(T x, T y) {
     if constexpr (std::is_floating_point<T>::value) {
-        if (a != a) return a;
-        if (b != b) return b;
-        if (a == b) return signbit(a) ? a : b;  // -0.0 under +0.0
+        const bool take_y = (y < x) | (signbit(y) > signbit(x));
+        const T yy = (x != x) ? x : y;
+        const T xx = (y != y) ? y : x;
+        return take_y ? yy : xx;
+    } else {
+        return x < y ? x : y;
     }
-    return a < b ? a : b;
 }
 
 template <class T, class Op>
@@ -60,6 +69,8 @@ struct Traits<T, JAdd> {
                                   typename std::conditional<std::is_signed<T>::value, int64_t, uint64_t>::type,
                                   T>::type>::type;
     using R = typename std::conditional<std::is_same<T, float>::value, float, A>::type;
+    __host__ __device__ static __forceinline__ A lift(T x) { return (A)x; }
+    __host__ __device__ static __forceinline__ R lower(A a) { return (R)a; }
     __device__ static __forceinline__ A identity() { return A(0); }
     __device__ static __forceinline__ A op(A a, A b) { return jadd(a, b); }
 };
@@ -77,21 +88,55 @@ __device__ __forceinline__ T highest_of() {
     else return (T)~T(0);
 }
 
-template <class T>
-struct Traits<T, JMax> {
-    using A = T;
+// Order-preserving unsigned keys of a float (Base.isless order with -0.0 < +0.0).  A NaN maps to
+// the key that wins (all ones for max, zero for min), so max/min of floats run as integer
+// max/min: one instruction per step instead of Base.max's select chain.  Keys are converted back
+// once, at the output (a NaN result comes back as the canonical quiet NaN).
+template <class F>
+struct FloatKey {
+    using K = typename std::conditional<sizeof(F) == 4, uint32_t, uint64_t>::type;
+    static constexpr K kSign = (K)1 << (8 * sizeof(F) - 1);
+    __host__ __device__ static __forceinline__ K key(F x, bool for_max) {
+        K b;
+        memcpy(&b, &x, sizeof(F));
+        if (x != x) return for_max ? (K)~(K)0 : (K)0;
+        return (b & kSign) ? (K)~b : (K)(b | kSign);
+    }
+    __host__ __device__ static __forceinline__ F value(K k, bool for_max) {
+        if (k == (for_max ? (K)~(K)0 : (K)0)) return F(NAN);
+        const K b = (k & kSign) ? (K)(k & ~kSign) : (K)~k;
+        F x;
+        memcpy(&x, &b, sizeof(F));
+        return x;
+    }
+};
+
+template <class T, bool MAX>
+struct MaxMinTraits {
+    static constexpr bool kFloat = std::is_floating_point<T>::value;
+    using A = typename std::conditional<kFloat, typename FloatKey<typename std::conditional<kFloat, T, float>::type>::K,
+                                        T>::type;
     using R = T;
-    __device__ static __forceinline__ A identity() { return lowest_of<T>(); }
-    __device__ static __forceinline__ A op(A a, A b) { return jmax(a, b); }
+    __host__ __device__ static __forceinline__ A lift(T x) {
+        if constexpr (kFloat) return FloatKey<T>::key(x, MAX);
+        else return x;
+    }
+    __host__ __device__ static __forceinline__ R lower(A a) {
+        if constexpr (kFloat) return FloatKey<T>::value(a, MAX);
+        else return a;
+    }
+    __device__ static __forceinline__ A identity() {  // key of -Inf / +Inf; lowest / highest integer
+        if constexpr (kFloat) return lift(MAX ? (T)-INFINITY : (T)INFINITY);
+        else return MAX ? lowest_of<T>() : highest_of<T>();
+    }
+    __device__ static __forceinline__ A op(A a, A b) { return MAX ? (a > b ? a : b) : (a < b ? a : b); }
 };
 
 template <class T>
-struct Traits<T, JMin> {
-    using A = T;
-    using R = T;
-    __device__ static __forceinline__ A identity() { return highest_of<T>(); }
-    __device__ static __forceinline__ A op(A a, A b) { return jmin(a, b); }
-};
+struct Traits<T, JMax> : MaxMinTraits<T, true> {};
+
+template <class T>
+struct Traits<T, JMin> : MaxMinTraits<T, false> {};
 
 // Functor form for the warp folds and scans of ki/intrinsics.cuh.
 template <class T, class Op>

@@ -41,9 +41,9 @@ __device__ __forceinline__ typename ki::Traits<T, Op>::A fold_vec(const ki::Vec1
     if constexpr (std::is_same<T, float>::value && std::is_same<Op, ki::JAdd>::value) {
         return (double)((v.v[0] + v.v[1]) + (v.v[2] + v.v[3]));
     } else {
-        A r = (A)v.v[0];
+        A r = Tr::lift(v.v[0]);
 #pragma unroll
-        for (int i = 1; i < kV; ++i) r = Tr::op(r, (A)v.v[i]);
+        for (int i = 1; i < kV; ++i) r = Tr::op(r, Tr::lift(v.v[i]));
         return r;
     }
 }
@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(kThreads)
     if (blockIdx.x == 0) {
         const size_t tail0 = head + nvec * kVec;
         const int t = threadIdx.x;
-        if ((size_t)t < head) acc = Tr::op(acc, (A)x[t]);
-        if ((size_t)t < n - tail0) acc = Tr::op(acc, (A)x[tail0 + t]);
+        if ((size_t)t < head) acc = Tr::op(acc, Tr::lift(x[t]));
+        if ((size_t)t < n - tail0) acc = Tr::op(acc, Tr::lift(x[tail0 + t]));
     }
     A bsum = block_fold(acc, sm, f, id);
     if (threadIdx.x == 0) {
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads)
     r = block_fold(r, sm, f, id);
     if (threadIdx.x == 0) {
         if (out_acc) *out_acc = r;
-        if (out) *out = (typename Tr::R)r;
+        if (out) *out = Tr::lower(r);
         *ticket = 0u;  // ready for the next call on this stream
     }
 }

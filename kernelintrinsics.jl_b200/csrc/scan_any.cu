@@ -9,8 +9,9 @@
 //   * values are accumulated in Traits<T, Op>::A (ki/ops.cuh: 64-bit integers for Int32/UInt32 sums,
 //     Float64 for Float32 sums) and written as Traits<T, Op>::R (Int64/UInt64 for widened sums,
 //     Float32 for Float32 sums, T otherwise), as Base.cumsum does;
-//   * tile aggregates and prefixes travel through the lookback's side arrays
-//     (decoupled_lookback_wide in ki/lookback.cuh), since a value of any type needs all its bits.
+//   * tile aggregates and prefixes ride in the status words when they fit (4-byte values, 8-byte
+//     integers within 61 bits) and otherwise travel through the lookback's side arrays
+//     (decoupled_lookback_any in ki/lookback.cuh).
 // The Int64 + scan keeps its own kernel (scan.cu), whose values travel packed in the status words.
 //
 // Exclusive scans write op(init, x[1..i-1]) at i (init at the first element); inclusive scans
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
         if (w == kLookWarp) {
             if (have_old) {
                 PendingAny<A>& o = slot[cur ^ 1];
-                const A ex = ki::decoupled_lookback_wide<1>(a.st, o.t, o.agg, init, id, op, a.status, a.timeout_ns);
+                const A ex = ki::decoupled_lookback_any<1>(a.st, o.t, o.agg, init, id, op, a.status, a.timeout_ns);
                 if (lane == 0) o.tile_excl = ex;
             }
         } else if (new_valid) {
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             for (int j = 0; j < kRowsPerWarp; ++j) {
                 const ki::Vec16<T> v = *reinterpret_cast<const ki::Vec16<T>*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
 #pragma unroll
-                for (int e = 0; e < kE; ++e) s = op(s, (A)v.v[e]);
+                for (int e = 0; e < kE; ++e) s = op(s, Tr::lift(v.v[e]));
             }
             s = ki::warpfold(s, op);
             if (lane == 0) warp_tot[w] = s;
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 if (lane == 0) {
                     e.t = t_new;
                     e.agg = agg;
-                    ki::publish_aggregate_wide(a.st, t_new, agg, init, op);
+                    ki::publish_aggregate_any(a.st, t_new, agg, init, op);
                 }
             }
         }
@@ -189,9 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
 #pragma unroll
             for (int j = 0; j < kRowsPerWarp; ++j) {
                 A part[kE];  // inclusive prefixes of this lane's elements
-                part[0] = (A)v[j].v[0];
+                part[0] = Tr::lift(v[j].v[0]);
 #pragma unroll
-                for (int e = 1; e < kE; ++e) part[e] = op(part[e - 1], (A)v[j].v[e]);
+                for (int e = 1; e < kE; ++e) part[e] = op(part[e - 1], Tr::lift(v[j].v[e]));
                 const A inc = ki::warpreduce(part[kE - 1], op);
                 A before = __shfl_up_sync(0xffffffffu, inc, 1);
                 if (lane == 0) before = id;
@@ -199,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 alignas(16) R r[kE];
 #pragma unroll
                 for (int e = 0; e < kE; ++e) {
-                    if (EXCL) r[e] = (R)(e == 0 ? base : op(base, part[e - 1]));
-                    else r[e] = (R)op(base, part[e]);
+                    if (EXCL) r[e] = Tr::lower(e == 0 ? base : op(base, part[e - 1]));
+                    else r[e] = Tr::lower(op(base, part[e]));
                 }
                 const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
                 if (full && a.vec_out) {
@@ -239,13 +240,17 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, size_t n,
     if (h_init) {
         R r;
         memcpy(&r, h_init, sizeof(R));
-        init = (A)r;
+        if constexpr (std::is_same<Op, ki::JAdd>::value) init = (A)r;
+        else init = Tr::lift(r);
     } else if constexpr (std::is_same<Op, ki::JAdd>::value) {
         init = A(0);
-    } else if constexpr (std::is_same<Op, ki::JMax>::value) {
-        init = std::is_floating_point<A>::value ? (A)-INFINITY : std::numeric_limits<A>::lowest();
     } else {
-        init = std::is_floating_point<A>::value ? (A)INFINITY : std::numeric_limits<A>::max();
+        using TT = typename std::conditional<std::is_floating_point<T>::value, T, double>::type;
+        if constexpr (std::is_floating_point<T>::value)
+            init = Tr::lift(std::is_same<Op, ki::JMax>::value ? -std::numeric_limits<TT>::infinity()
+                                                               : std::numeric_limits<TT>::infinity());
+        else
+            init = std::is_same<Op, ki::JMax>::value ? std::numeric_limits<A>::lowest() : std::numeric_limits<A>::max();
     }
     const size_t ntiles = (n + S::kTile - 1) / S::kTile;
     const size_t words_off = 256;

@@ -8,6 +8,7 @@ every relative misalignment.  Every rank copies its own buffers (weak scaling, n
 The same line carries, under "kernels", the other device-wide primitives on their own workloads:
   reduce   Float32 sum, n = 2^24 (L2 flushed between steps; inputs are smaller than L2)
   scan     Int64 inclusive scan, n = 2^30, range-sharded over the ranks + NCCL all-gather of totals
+  scan_f32 Float32 cumsum (generic scan, Float64 accumulation), n = 2^28 per rank
   compact  filter/findall of x > 0.5 over 2^28 N(0,1) Float32, range-sharded + all-gather of counts
   gemm     fp8 e4m3 GEMM 8192^3 with Float32 output (replicas at N > 1)
 
@@ -35,6 +36,7 @@ sys.path.insert(0, str(REPO / "kernelintrinsics.jl_b200"))
 COPY_BYTES = 1 << 28
 REDUCE_N = 1 << 24
 SCAN_N = 1 << 30
+SCAN_F32_N = 1 << 28
 COMPACT_N = 1 << 28
 GEMM_MNK = 8192
 L2_FLUSH_BYTES = 256 << 20
@@ -459,6 +461,27 @@ def bench_scan(KI, D, steps, warmup, hbm):
             "bytes_moved_per_elem": 16 if D.world == 1 else 24, "l2": "inputs larger than L2"}
 
 
+def bench_scan_f32(KI, D, steps, warmup, hbm):
+    """Float32 cumsum (ki_scan, Float64 accumulation) of 2^28 uniform[0,1) values per rank; the
+    per-rank scans are independent (a replica per rank, weak scaling)."""
+    import torch
+
+    n = SCAN_F32_N
+    dev = torch.device("cuda", D.dev)
+    x = torch.empty(n, dtype=torch.float32, device=dev)
+    KI.fill_uniform(x, seed=1 + D.rank)
+    y = torch.empty_like(x)
+    stream = torch.cuda.current_stream(dev)
+    mean_ms, med_ms = _timed_steps(D, stream, lambda: KI.scan(x, "+", out=y), steps, warmup)
+    KI.context(D.dev).check()
+    gbs = 8 * n * D.world / (mean_ms * 1e-3) / 1e9
+    del x, y
+    torch.cuda.empty_cache()
+    return {"workload": "Float32 inclusive scan (cumsum) n=2^28 per rank, Float64 accumulation", "value": round(gbs, 2),
+            "unit": "GB/s", "ms_per_step": round(mean_ms, 4), "frac_of_hbm_per_gpu": round(gbs / D.world / hbm, 4),
+            "algorithmic_bytes": 8 * n, "replicas": D.world, "l2": "inputs larger than L2"}
+
+
 def bench_compact(KI, D, steps, warmup, hbm):
     import torch
 
@@ -632,6 +655,7 @@ def main():
             only = set(filter(None, args.only.split(",")))
             plan = [("reduce", lambda: bench_reduce(KI, D, 50, 5, hbm)),
                     ("scan", lambda: bench_scan(KI, D, 10, 3, hbm)),
+                    ("scan_f32", lambda: bench_scan_f32(KI, D, 10, 3, hbm)),
                     ("compact", lambda: bench_compact(KI, D, 20, 3, hbm)),
                     ("gemm", lambda: bench_gemm(KI, D, 20, 3, bf16))]
             for name, fn in plan:

@@ -118,6 +118,12 @@ int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out,
  * as Base.max / Base.min).  n = 0: KI_OP_ADD writes zero, KI_OP_MAX / KI_OP_MIN return KI_ERR_ARG
  * (Base throws on an empty maximum).  Deterministic for a given n and device. */
 int ki_reduce(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t n, void* d_out, void* stream);
+/* Segmented reduce: one ki_reduce per row of a row-major rows x cols matrix whose rows start ld
+ * elements apart (ld >= cols; a column-major Julia matrix reduced along dims=1 has rows = its
+ * columns).  d_out receives rows values of ki_reduce's result type.  cols = 0: KI_OP_ADD writes
+ * zeros, KI_OP_MAX / KI_OP_MIN return KI_ERR_ARG.  Deterministic for a given shape and device. */
+int ki_reduce_rows(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t rows, size_t cols, size_t ld,
+                   void* d_out, void* stream);
 
 /* ---- (a4/a5) single-pass decoupled-lookback inclusive scan ----------------------------------
  * Replaces: @warpreduce (src/warp.jl:226-237) for the in-warp scan, @access / @fence

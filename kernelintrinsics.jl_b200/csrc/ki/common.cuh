@@ -24,7 +24,9 @@ enum ki_region {
     KI_REG_MISC = 3,
     KI_REG_STAGE = 4,  // device staging slots of the host-buffer copy
     KI_REG_SCAN_ANY = 5,  // the generic scan (any operator and type)
-    KI_REG_COUNT = 6
+    KI_REG_ROWS = 6,       // per-row tickets of the segmented reduce
+    KI_REG_ROWS_PART = 7,  // per-row partials of the segmented reduce
+    KI_REG_COUNT = 8
 };
 
 // Host-buffer copy pipeline: slots of staging memory cycled over three streams.

@@ -30,7 +30,7 @@ __all__ = [
     "Up", "Down", "Xor", "Idx", "All", "AnyLane", "Uni", "Ballot", "KIError", "KIArgumentError",
     "KITimeoutError", "Context", "context", "warpsize", "get_warpsize", "devices", "shfl", "warpreduce",
     "warpfold", "vote", "vload", "vstore", "vload_multi", "vstore_multi", "generate_partN", "access",
-    "message_pass", "vcopy", "vcopy_host", "reduce", "scan", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
+    "message_pass", "vcopy", "vcopy_host", "reduce", "reduce_rows", "scan", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
     "fp8_gemm", "fill_uniform", "fill_int_range", "fill_bytes", "fill_normal", "fill_e4m3_uniform",
 ]
 
@@ -497,6 +497,23 @@ def reduce(x, op: str = "+", out=None, stream=None):
     x = x.contiguous()
     out = torch.empty((), dtype=_result_dtype(x.dtype, op), device=x.device) if out is None else out
     context(d).call("ki_reduce", _GENERIC_OPS[op], _dtype_code(x), _ptr(x), x.numel(), _ptr(out),
+                    _stream_ptr(stream, d))
+    return out
+
+
+def reduce_rows(x, op: str = "+", out=None, stream=None):
+    """One sum / maximum / minimum per row of a 2-D ``x`` whose rows are contiguous (``x.stride(1) == 1``;
+    ``x.stride(0)`` is the leading dimension).  Result types as ``reduce``."""
+    torch = _torch()
+    d = _dev(x)
+    if op not in _GENERIC_OPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"reduce_rows: op must be one of {sorted(_GENERIC_OPS)}")
+    if x.dim() != 2 or (x.shape[1] > 1 and x.stride(1) != 1):
+        raise KIArgumentError(_abi.KI_ERR_ARG, "reduce_rows: 2-D input with contiguous rows")
+    rows, cols = x.shape
+    ld = x.stride(0) if rows > 1 else cols
+    out = torch.empty(rows, dtype=_result_dtype(x.dtype, op), device=x.device) if out is None else out
+    context(d).call("ki_reduce_rows", _GENERIC_OPS[op], _dtype_code(x), _ptr(x), rows, cols, max(ld, cols), _ptr(out),
                     _stream_ptr(stream, d))
     return out
 

@@ -149,3 +149,38 @@ def test_scan_config_size_f32(KI, dev):
     assert rel <= 1e-5 * 28, rel
     del x, y, ref
     torch.cuda.empty_cache()
+
+
+ROW_SHAPES = [(1, 1), (3, 5), (1000, 33), (257, 2048), (7, 2049), (5, 100_003), (2, (1 << 21) + 5), (600, 4096)]
+
+
+@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("op", OPS)
+def test_reduce_rows(KI, oracle, dev, dt, op):
+    """Segmented reduce (one result per row), with padded rows (ld > cols) and unaligned starts."""
+    for k, (rows, cols) in enumerate(ROW_SHAPES):
+        for pad in (0, 3):
+            ld = cols + pad
+            flat = _data(dt, rows * ld + 1, 1000 + k, op)
+            m = flat[1:].reshape(rows, ld) if pad else flat[: rows * ld].reshape(rows, ld)
+            xd = _to_dev(flat, dev)
+            view = (xd[1:] if pad else xd[: rows * ld]).view(rows, ld)[:, :cols]
+            got = KI.reduce_rows(view, op).cpu().numpy()
+            for r in range(rows) if rows <= 64 else range(0, rows, max(1, rows // 64)):
+                want = np.array([oracle.reduce_op(op, m[r, :cols])])
+                g = got[r:r + 1]
+                if np.dtype(dt).kind == "f" and op == "+":
+                    bound = 1e-5 * math.log2(max(2, cols)) * float(np.abs(m[r, :cols].astype(np.float64)).sum())
+                    assert abs(float(g[0]) - float(want[0])) <= bound, (rows, cols, r)
+                else:
+                    _check(g, want.astype(g.dtype), m[r, :cols], op)
+    KI.context(0).check()
+
+
+def test_reduce_rows_empty_rows(KI, dev):
+    import torch
+
+    x = torch.empty((4, 0), dtype=torch.float32, device=dev)
+    assert KI.reduce_rows(x, "+").tolist() == [0.0] * 4
+    with pytest.raises(KI.KIArgumentError):
+        KI.reduce_rows(x, "max")

@@ -3,8 +3,9 @@
 // column-major Julia matrix, one result per column).
 //
 // The same operators, types and result types as ki_reduce (ki/ops.cuh).  Two kernels:
-//   * short rows (cols <= 2048): one warp per row, lanes stride the row with coalesced loads and the
-//     warp folds with __shfl_xor_sync (@warpfold); 8 rows per 256-thread block;
+//   * short rows (cols <= 2048): persistent warps, folding rows of up to 1 KiB 4 at a time and longer
+//     ones one at a time (16-byte vectors when the rows allow, lanes striding the row) with
+//     __shfl_xor_sync (@warpfold);
 //   * long rows: each row is cut into chunks, one 256-thread block per chunk streams it (16-byte
 //     vectors when the rows allow, 4 in flight per thread), folds it like the device-wide reduce and
 //     writes a partial; the last block of a row (per-row atomic ticket after a release fence) folds
@@ -22,20 +23,58 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 4;
 constexpr size_t kShortRow = 2048;  // rows up to this many elements take one warp each
 
-template <class T, class Op>
+// Short rows: persistent warps.  Rows of at most 1 KiB are taken RPP = 4 at a time so that several
+// rows' loads are in flight (a 128-element Float32 row is one 16-byte load per lane); longer rows
+// one at a time with 4 vectors per lane in flight.
+template <class T, class Op, bool VEC, int RPP>
 __global__ void __launch_bounds__(kThreads) rows_warp_kernel(const T* __restrict__ x, size_t rows, size_t cols,
                                                              size_t ld, typename ki::Traits<T, Op>::R* out) {
     using Tr = ki::Traits<T, Op>;
     using A = typename Tr::A;
+    using V = ki::Vec16<T>;
+    constexpr int kVec = (int)(16 / sizeof(T));
     const ki::OpFn<T, Op> f;
-    const size_t row = (size_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
     const unsigned lane = threadIdx.x & 31;
-    if (row >= rows) return;  // whole warps leave together
-    const T* xr = x + row * ld;
-    A acc = Tr::identity();
-    for (size_t c = lane; c < cols; c += 32) acc = Tr::op(acc, Tr::lift(__ldcs(xr + c)));
-    acc = ki::warpfold(acc, f);
-    if (lane == 0) out[row] = Tr::lower(acc);
+    const size_t nwarps = (size_t)gridDim.x * kWarps;
+    const size_t nvec = VEC ? cols / kVec : 0;
+    constexpr int kIn = RPP == 1 ? 4 : 1;  // vectors per lane and row in flight
+    for (size_t r0 = ((size_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * RPP; r0 < rows; r0 += nwarps * RPP) {
+        A acc[RPP];
+#pragma unroll
+        for (int u = 0; u < RPP; ++u) acc[u] = Tr::identity();
+        if (VEC) {  // rows start on 16-byte boundaries
+            for (size_t i0 = lane; i0 < nvec; i0 += 32 * kIn) {
+                V v[RPP][kIn];
+#pragma unroll
+                for (int u = 0; u < RPP; ++u)
+#pragma unroll
+                    for (int q = 0; q < kIn; ++q) {
+                        const size_t i = i0 + 32 * q;
+                        if (r0 + u < rows && i < nvec) {
+                            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(x + (r0 + u) * ld) + i);
+                            v[u][q] = *reinterpret_cast<const V*>(&raw);
+                        }
+                    }
+#pragma unroll
+                for (int u = 0; u < RPP; ++u)
+#pragma unroll
+                    for (int q = 0; q < kIn; ++q)
+                        if (r0 + u < rows && i0 + 32 * q < nvec)
+#pragma unroll
+                            for (int e = 0; e < kVec; ++e) acc[u] = Tr::op(acc[u], Tr::lift(v[u][q].v[e]));
+            }
+        }
+        for (size_t c = nvec * kVec + lane; c < cols; c += 32) {
+#pragma unroll
+            for (int u = 0; u < RPP; ++u)
+                if (r0 + u < rows) acc[u] = Tr::op(acc[u], Tr::lift(__ldcs(x + (r0 + u) * ld + c)));
+        }
+#pragma unroll
+        for (int u = 0; u < RPP; ++u) {
+            const A a = ki::warpfold(acc[u], f);
+            if (lane == 0 && r0 + u < rows) out[r0 + u] = Tr::lower(a);
+        }
+    }
 }
 
 template <class T, class Op, bool VEC>
@@ -121,9 +160,17 @@ int rows_launch(ki_ctx* ctx, const void* d_x, size_t rows, size_t cols, size_t l
     const T* x = static_cast<const T*>(d_x);
     R* out = static_cast<R*>(d_out);
     if (cols <= kShortRow) {
-        const size_t blocks = (rows + kWarps - 1) / kWarps;
-        if (blocks > 0x7fffffffull) return ki::set_error(ctx, KI_ERR_ARG, "reduce_rows: too many rows");
-        rows_warp_kernel<T, Op><<<(unsigned)blocks, kThreads, 0, s>>>(x, rows, cols, ld, out);
+        const bool vec = ki::aligned(d_x, 16) && (ld * sizeof(T)) % 16 == 0;
+        const bool multi = cols * sizeof(T) <= 1024;
+        const size_t rpp = multi ? 4 : 1;
+        size_t blocks = (rows + (size_t)kWarps * rpp - 1) / ((size_t)kWarps * rpp);
+        const size_t max_blocks = (size_t)ctx->sm_count * 8;
+        if (blocks > max_blocks) blocks = max_blocks;
+        const unsigned g = (unsigned)blocks;
+        if (vec && multi) rows_warp_kernel<T, Op, true, 4><<<g, kThreads, 0, s>>>(x, rows, cols, ld, out);
+        else if (vec) rows_warp_kernel<T, Op, true, 1><<<g, kThreads, 0, s>>>(x, rows, cols, ld, out);
+        else if (multi) rows_warp_kernel<T, Op, false, 4><<<g, kThreads, 0, s>>>(x, rows, cols, ld, out);
+        else rows_warp_kernel<T, Op, false, 1><<<g, kThreads, 0, s>>>(x, rows, cols, ld, out);
         return ki::check_launch(ctx, "rows_warp_kernel launch");
     }
     // chunks per row: fill ~8 blocks per SM, but keep each chunk at least 4 vectors per thread

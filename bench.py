@@ -62,7 +62,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="", help="comma list of kernels to run under 'kernels'")
-    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm"],
+    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm", "scan_f32", "rows"],
                    help="run only this kernel, --profile-launches times, on a small case (for ncu)")
     p.add_argument("--profile-n", type=int, default=0, help="elements (bytes for copy; M=N=K for gemm)")
     p.add_argument("--profile-launches", type=int, default=3)
@@ -109,6 +109,20 @@ def run_profile(args):
         c = torch.zeros((), dtype=torch.uint64, device=dev)
         fn = lambda: KI.vote_compact(x, 0.5, out_vals=v, out_idx=i, count=c, trim=False)
         alg = 4 * n + 8 * int(0.30854 * n)
+    elif k == "scan_f32":
+        n = n or (1 << 26)
+        x = torch.empty(n, dtype=torch.float32, device=dev)
+        KI.fill_uniform(x, seed=1)
+        y = torch.empty_like(x)
+        fn = lambda: KI.scan(x, "+", out=y)
+        alg = 8 * n
+    elif k == "rows":
+        n = n or 8192  # n x n Float32, one sum per row
+        x = torch.empty((n, n), dtype=torch.float32, device=dev)
+        KI.fill_uniform(x.view(-1), seed=1)
+        y = torch.empty(n, dtype=torch.float32, device=dev)
+        fn = lambda: KI.reduce_rows(x, "+", out=y)
+        alg = 4 * n * n
     else:
         n = n or 4096
         A = torch.empty((n, n), dtype=torch.uint8, device=dev)

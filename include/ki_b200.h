@@ -163,6 +163,14 @@ int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out, size_t n,
  * index_base + n - 1 <= INT32_MAX and index_base >= INT32_MIN. */
 int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float threshold, float* d_out_vals,
                       int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream);
+/* Compaction for any comparison predicate and element type (the same @vote Ballot pipeline):
+ * filter(v -> v op t, x) and findall(v -> v op t, x) with op one of ki_pred, IEEE comparisons for
+ * floats (a NaN is never kept except by KI_PRED_NE), dtype KI_I32, KI_U32, KI_I64, KI_U64, KI_F32 or
+ * KI_F64, h_thr a host pointer to one value of dtype; d_out_vals holds values of dtype, d_out_idx
+ * Int32 indices starting at index_base; either output may be NULL. */
+typedef enum { KI_PRED_GT = 0, KI_PRED_GE = 1, KI_PRED_LT = 2, KI_PRED_LE = 3, KI_PRED_EQ = 4, KI_PRED_NE = 5 } ki_pred;
+int ki_compact(ki_ctx* ctx, int pred, int dtype, const void* d_x, size_t n, const void* h_thr, void* d_out_vals,
+               int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream);
 
 /* ---- (a8) fp8 e4m3 GEMM on tcgen05 / TMEM ---------------------------------------------------
  * No counterpart in the reference.  C = (scale_a * scale_b) * A * B with A: M x K row-major e4m3,

@@ -1,6 +1,9 @@
-// compact.cu -- order-preserving stream compaction: filter(x -> x > t, x) and findall.
+// compact.cu -- order-preserving stream compaction: filter(v -> v op t, x) and findall(v -> v op t, x)
+// for op in >, >=, <, <=, ==, != over Int32, UInt32, Int64, UInt64, Float32 and Float64 (IEEE
+// comparisons, as Base's operators).
 //
-// Persistent CTAs (3 per SM), software-pipelined over tiles of 16384 elements, with 8 "work" warps
+// Persistent CTAs (3 per SM), software-pipelined over 64 KiB tiles (16384 4-byte or 8192 8-byte
+// elements; the description below counts 4-byte elements), with 8 "work" warps
 // and one "look" warp, the same pipeline as scan.cu.  Iteration k of a CTA runs two phases:
 //   phase A  work warps: wait for tile k (one 64 KiB 1-D TMA bulk copy, cp.async.bulk ...
 //            mbarrier::complete_tx) and count its kept elements (warp w owns 2048 elements as 16 rows
@@ -18,8 +21,8 @@
 //            goes to its lane's discard slot, so there are no branches) and leave as coalesced
 //            evict-first stores at tile prefix + warp prefix + row prefix.
 // Between taking a ticket and publishing that tile's count a CTA only waits for its own load and
-// its own second pass, never for a lookback.  Tiles that are partial or not 16-byte aligned are read
-// with plain loads (padded with -Inf, which is never kept).
+// its own second pass, never for a lookback.  Tiles that are not 16-byte aligned are read with plain
+// loads; in the partial last tile, elements past the end are excluded explicitly.
 //
 // Measured at n = 2^28 (0.467 ms, 0.57 of the copy peak): without the stores the same kernel takes
 // 0.235 ms.  Writing the output streams evicts tiles that wait for their prefix, so most second-pass
@@ -30,44 +33,51 @@
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
+#include "ki/ops.cuh"
 
 namespace {
 
 #ifndef KI_COMPACT_LOOKBACK_K
 #define KI_COMPACT_LOOKBACK_K 1
 #endif
-#ifndef KI_COMPACT_TILE
-#define KI_COMPACT_TILE 16384
-#endif
 #ifndef KI_COMPACT_CTAS_PER_SM
 #define KI_COMPACT_CTAS_PER_SM 3
 #endif
-#ifndef KI_COMPACT_WORK_WARPS
-#define KI_COMPACT_WORK_WARPS 8
-#endif
-constexpr int kWorkWarps = KI_COMPACT_WORK_WARPS;
+constexpr int kWorkWarps = 8;
 constexpr int kLookWarp = kWorkWarps;
 constexpr int kWorkThreads = 32 * kWorkWarps;
 constexpr int kThreads = kWorkThreads + 32;
-constexpr int kTile = KI_COMPACT_TILE;
-constexpr int kWarpSpan = kTile / kWorkWarps;   // elements per work warp
-constexpr int kRows = kWarpSpan / 128;          // rows of 32 lanes x float4
-static_assert(kWarpSpan % 128 == 0 && kWorkWarps <= 32, "tile must split into rows of 128 elements per warp");
-constexpr int kBatch = kRows < 8 ? kRows : 8;   // rows loaded at once in the second pass
-static_assert(kRows % kBatch == 0, "rows must split into whole batches");
-// per warp: 128 values + 32 discard slots, then 128 indices + 32 discard slots
-constexpr int kStageSlots = 160;
-constexpr size_t kStageBytes = (size_t)kWorkWarps * kStageSlots * 8;
-constexpr size_t kTileBytes = (size_t)kTile * sizeof(float);
-constexpr size_t kSmemBytes = kTileBytes + kStageBytes;
+constexpr size_t kTileBytes = 65536;  // 16384 elements of 4 bytes or 8192 of 8
+constexpr int kRows = 16;             // rows of 32 lanes x one 16-byte vector per work warp
+constexpr int kBatch = 8;             // rows loaded at once in the second pass
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 
+template <class T>
+struct CShape {
+    static constexpr int kE = (int)(16 / sizeof(T));         // elements per lane per row
+    static constexpr int kRow = 32 * kE;                      // elements per row
+    static constexpr int kSpan = kRows * kRow;                 // elements per work warp
+    static constexpr int kTile = kWorkWarps * kSpan;           // elements per tile
+    static constexpr int kStageSlots = kRow + 32;              // a row's run + one discard slot per lane
+    static constexpr size_t kStageBytes = (size_t)kWorkWarps * kStageSlots * (sizeof(T) + sizeof(int32_t));
+    static constexpr size_t kSmemBytes = kTileBytes + kStageBytes;
+    static_assert(kTile * sizeof(T) == kTileBytes, "tile layout");
+};
+
+// Comparison predicates (x op t), IEEE semantics for floats as Base's <, <=, ==, != and >.
+struct PGt { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x > t; } };
+struct PGe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x >= t; } };
+struct PLt { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x < t; } };
+struct PLe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x <= t; } };
+struct PEq { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x == t; } };
+struct PNe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x != t; } };
+
 struct CompactArgs {
-    const float* x;
+    const void* x;
     size_t n;
-    float thr;
-    float* out_vals;
+    uint64_t thr_bits;  // the threshold, as a T
+    void* out_vals;
     int32_t* out_idx;
     int64_t index_base;
     uint64_t* d_count;
@@ -75,7 +85,7 @@ struct CompactArgs {
     unsigned long long* ticket;
     uint32_t* status;
     uint64_t timeout_ns;
-    int tma_in;  // x is 16-byte aligned: full tiles come in by TMA, rows by float4
+    int tma_in;  // x is 16-byte aligned: full tiles come in by TMA, rows as 16-byte vectors
 };
 
 struct Pending {
@@ -87,20 +97,23 @@ struct Pending {
 
 __device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
 
-__device__ __forceinline__ int kept4(const float4& v, float thr) {
-    return (v.x > thr) + (v.y > thr) + (v.z > thr) + (v.w > thr);
-}
-
-// VALS / IDX: which outputs are written (an absent output costs no instructions).
-template <bool VALS, bool IDX>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(CompactArgs a) {
+// T: element type; P: predicate; VALS / IDX: which outputs are written (an absent output costs no
+// instructions).
+template <class T, class P, bool VALS, bool IDX>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactArgs a) {
+    using S = CShape<T>;
+    using V = ki::Vec16<T>;
+    constexpr int kE = S::kE;
+    constexpr int kTile = S::kTile;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    float* sb = reinterpret_cast<float*>(smem_raw);
+    T* sb = reinterpret_cast<T*>(smem_raw);
     __shared__ __align__(8) uint64_t bar;
     __shared__ int warp_cnt[kWorkWarps];
     __shared__ Pending slot[2];  // tile k (being counted) and tile k-1 (being written)
     __shared__ unsigned long long ticket;
 
+    const T* x = static_cast<const T*>(a.x);
+    const T thr = ki::from_bits<T>(a.thr_bits);
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
@@ -112,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(Co
         if (bulk_ok(t)) {
             ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
             ki::mbar_arrive_expect_tx(&bar, (uint32_t)kTileBytes);
-            ki::bulk_g2s(sb, a.x + t * kTile, (uint32_t)kTileBytes, &bar);
+            ki::bulk_g2s(sb, x + t * kTile, (uint32_t)kTileBytes, &bar);
         }
     };
     if (tid == 0) {
@@ -123,7 +136,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(Co
     __syncthreads();
 
     const unsigned below = (1u << lane) - 1u;  // lanes with a lower index
-    const float thr = a.thr;
     uint32_t phase = 0;
     bool have_old = false;
     int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
@@ -137,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(Co
             if (have_old) {
                 Pending& o = slot[cur ^ 1];
                 // bring tile k-1 back into L2 (if it left) while its prefix is looked up
-                if (lane == 0 && bulk_ok(o.t)) ki::bulk_prefetch_l2(a.x + o.t * kTile, (uint32_t)kTileBytes);
+                if (lane == 0 && bulk_ok(o.t)) ki::bulk_prefetch_l2(x + o.t * kTile, (uint32_t)kTileBytes);
                 const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, 0, a.status, a.timeout_ns);
                 if (lane == 0) o.tile_excl = ex;
             }
@@ -149,23 +161,35 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(Co
                     ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
                 phase ^= 1u;
             } else {
-                // partial or unaligned tile: plain loads, padded with values that are never kept
-                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? a.x[first + i] : -INFINITY;
+                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? x[first + i] : T(0);
                 work_sync();
             }
-            const float4* row0 = reinterpret_cast<const float4*>(sb + w * kWarpSpan) + lane;
+            const V* row0 = reinterpret_cast<const V*>(sb + w * S::kSpan) + lane;
             int c = 0;
+            if (count == kTile) {
 #pragma unroll 8
-            for (int j = 0; j < kRows; ++j) c += kept4(row0[32 * j], thr);
+                for (int j = 0; j < kRows; ++j) {
+                    const V v = row0[32 * j];
+#pragma unroll
+                    for (int e = 0; e < kE; ++e) c += P::test(v.v[e], thr);
+                }
+            } else {  // the partial last tile: elements past count do not exist
+                const int i_lane = w * S::kSpan + kE * (int)lane;
+                for (int j = 0; j < kRows; ++j) {
+                    const V v = row0[32 * j];
+#pragma unroll
+                    for (int e = 0; e < kE; ++e) c += (i_lane + S::kRow * j + e < count) && P::test(v.v[e], thr);
+                }
+            }
             c = ki::warpfold(c, ki::Add{});
             if (lane == 0) warp_cnt[w] = c;
             work_sync();
             if (w == 0) {
-                const int x = (lane < (unsigned)kWorkWarps) ? warp_cnt[lane] : 0;
-                const int inc = ki::warpreduce(x, ki::Add{});
+                const int xx = (lane < (unsigned)kWorkWarps) ? warp_cnt[lane] : 0;
+                const int inc = ki::warpreduce(xx, ki::Add{});
                 const int agg = __shfl_sync(0xffffffffu, inc, kWorkWarps - 1);
                 Pending& e = slot[cur];
-                if (lane < (unsigned)kWorkWarps) e.warp_excl[lane] = inc - x;
+                if (lane < (unsigned)kWorkWarps) e.warp_excl[lane] = inc - xx;
                 if (lane == 0) {
                     e.t = t_new;
                     e.agg = agg;
@@ -181,65 +205,76 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(Co
             const Pending& o = slot[cur ^ 1];
             const size_t first = (size_t)o.t * kTile;
             const int count = (int)min((size_t)kTile, a.n - first);
-            const bool vec_in = a.tma_in && count == kTile;
+            const bool full = count == kTile;
+            const bool vec_in = a.tma_in;
             // outputs of this warp start at one pointer; offsets from it fit 32 bits
             const int64_t at = o.tile_excl + o.warp_excl[w];
-            float* vals = VALS ? a.out_vals + at : nullptr;
+            T* vals = VALS ? static_cast<T*>(a.out_vals) + at : nullptr;
             int32_t* idxs = IDX ? a.out_idx + at : nullptr;
-            const int i_lane = w * kWarpSpan + 4 * (int)lane;  // element of (row 0, component 0)
-            // output index of that element; unsigned, so the padding past the last element wraps
-            // harmlessly instead of overflowing (it is never stored)
+            const int i_lane = w * S::kSpan + kE * (int)lane;  // element of (row 0, component 0)
+            // output index of that element; unsigned, so indices past the last element wrap
+            // harmlessly instead of overflowing (they are never stored)
             const uint32_t ix0 = (uint32_t)((int64_t)first + a.index_base) + (uint32_t)i_lane;
-            float* sv = reinterpret_cast<float*>(smem_raw + kTileBytes) + w * 2 * kStageSlots;
-            int32_t* si = reinterpret_cast<int32_t*>(sv + kStageSlots);
+            T* sv = reinterpret_cast<T*>(smem_raw + kTileBytes) + (size_t)w * S::kStageSlots;
+            int32_t* si = reinterpret_cast<int32_t*>(smem_raw + kTileBytes + (size_t)kWorkWarps * S::kStageSlots * sizeof(T)) +
+                          (size_t)w * S::kStageSlots;
             int pos = 0;
+            // FULL: a whole tile (no element past the end), the common case, without bounds checks
+            auto rows_pass = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll 1
-            for (int j0 = 0; j0 < kRows; j0 += kBatch) {
-                float4 v[kBatch];
+                for (int j0 = 0; j0 < kRows; j0 += kBatch) {
+                    V v[kBatch];
 #pragma unroll
-                for (int j = 0; j < kBatch; ++j) {  // a batch of loads in flight first
-                    const int i0 = i_lane + 128 * (j0 + j);
-                    if (vec_in) {
-                        v[j] = *reinterpret_cast<const float4*>(a.x + first + i0);
-                    } else {
-                        v[j].x = (i0 + 0 < count) ? a.x[first + i0 + 0] : -INFINITY;
-                        v[j].y = (i0 + 1 < count) ? a.x[first + i0 + 1] : -INFINITY;
-                        v[j].z = (i0 + 2 < count) ? a.x[first + i0 + 2] : -INFINITY;
-                        v[j].w = (i0 + 3 < count) ? a.x[first + i0 + 3] : -INFINITY;
+                    for (int j = 0; j < kBatch; ++j) {  // a batch of loads in flight first
+                        const int i0 = i_lane + S::kRow * (j0 + j);
+                        if (FULL && vec_in) {
+                            const uint4 raw = *reinterpret_cast<const uint4*>(x + first + i0);
+                            v[j] = *reinterpret_cast<const V*>(&raw);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < kE; ++e) v[j].v[e] = (FULL || i0 + e < count) ? x[first + i0 + e] : T(0);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        const int i0 = i_lane + S::kRow * (j0 + j);
+                        bool p[kE];
+                        unsigned b[kE];
+                        int ahead = 0, row = 0;
+#pragma unroll
+                        for (int e = 0; e < kE; ++e) {
+                            p[e] = P::test(v[j].v[e], thr);
+                            if (!FULL) p[e] = p[e] && (i0 + e < count);
+                            b[e] = ki::ballot(p[e]);
+                            ahead += __popc(b[e] & below);
+                            row += __popc(b[e]);
+                        }
+                        const uint32_t ix = ix0 + (uint32_t)(S::kRow * (j0 + j));
+                        // the row's kept elements, in source order, as one run in this warp's stage
+                        // (an element that is not kept goes to the lane's discard slot: no branches) ...
+                        const int junk = S::kRow + (int)lane;
+                        int r = ahead;
+#pragma unroll
+                        for (int e = 0; e < kE; ++e) {
+                            const int at_e = p[e] ? r : junk;
+                            if (VALS) sv[at_e] = v[j].v[e];
+                            if (IDX) si[at_e] = (int32_t)(ix + (uint32_t)e);
+                            r += (int)p[e];
+                        }
+                        __syncwarp();
+                        // ... written out with consecutive lanes on consecutive addresses
+                        for (int q = (int)lane; q < row; q += 32) {
+                            if (VALS) __stcs(vals + pos + q, sv[q]);
+                            if (IDX) __stcs(idxs + pos + q, si[q]);
+                        }
+                        __syncwarp();
+                        pos += row;
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    const bool p0 = v[j].x > thr, p1 = v[j].y > thr, p2 = v[j].z > thr, p3 = v[j].w > thr;
-                    const unsigned b0 = ki::ballot(p0), b1 = ki::ballot(p1), b2 = ki::ballot(p2), b3 = ki::ballot(p3);
-                    const int ahead = __popc(b0 & below) + __popc(b1 & below) + __popc(b2 & below) + __popc(b3 & below);
-                    const int row = __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
-                    const uint32_t ix = ix0 + 128u * (uint32_t)(j0 + j);
-                    // the row's kept elements, in source order, as one run in this warp's stage ...
-                    const int r0 = ahead, r1 = r0 + (int)p0, r2 = r1 + (int)p1, r3 = r2 + (int)p2;
-                    const int junk = 128 + (int)lane;
-                    if (VALS) {
-                        sv[p0 ? r0 : junk] = v[j].x;
-                        sv[p1 ? r1 : junk] = v[j].y;
-                        sv[p2 ? r2 : junk] = v[j].z;
-                        sv[p3 ? r3 : junk] = v[j].w;
-                    }
-                    if (IDX) {
-                        si[p0 ? r0 : junk] = (int32_t)ix;
-                        si[p1 ? r1 : junk] = (int32_t)(ix + 1u);
-                        si[p2 ? r2 : junk] = (int32_t)(ix + 2u);
-                        si[p3 ? r3 : junk] = (int32_t)(ix + 3u);
-                    }
-                    __syncwarp();
-                    // ... written out with consecutive lanes on consecutive addresses
-                    for (int e = (int)lane; e < row; e += 32) {
-                        if (VALS) __stcs(vals + pos + e, sv[e]);
-                        if (IDX) __stcs(idxs + pos + e, si[e]);
-                    }
-                    __syncwarp();
-                    pos += row;
-                }
-            }
+            };
+            if (full) rows_pass(std::true_type{});
+            else rows_pass(std::false_type{});
             if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);
         }
         __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
@@ -248,27 +283,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_gt_f32_kernel(Co
     }
 }
 
-template <bool VALS, bool IDX>
+template <class T, class P, bool VALS, bool IDX>
 int launch_compact(ki_ctx* ctx, const CompactArgs& a, size_t grid, cudaStream_t s) {
-    KI_CUDA(ctx, cudaFuncSetAttribute(compact_gt_f32_kernel<VALS, IDX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)kSmemBytes));
-    compact_gt_f32_kernel<VALS, IDX><<<(unsigned)grid, kThreads, kSmemBytes, s>>>(a);
-    return ki::check_launch(ctx, "compact_gt_f32_kernel launch");
+    constexpr size_t smem = CShape<T>::kSmemBytes;
+    KI_CUDA(ctx, cudaFuncSetAttribute(compact_kernel<T, P, VALS, IDX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+    compact_kernel<T, P, VALS, IDX><<<(unsigned)grid, kThreads, smem, s>>>(a);
+    return ki::check_launch(ctx, "compact_kernel launch");
 }
 
-}  // namespace
-
-extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float threshold, float* d_out_vals,
-                                 int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream) {
-    KI_CHECK_CTX(ctx);
-    if (n > 0 && !d_x) return ki::set_error(ctx, KI_ERR_ARG, "compact: null input");
-    if (n > 0 && !ki::aligned(d_x, 4)) return ki::set_error(ctx, KI_ERR_ARG, "compact: misaligned Float32 input");
-    if ((d_out_vals && !ki::aligned(d_out_vals, 4)) || (d_out_idx && !ki::aligned(d_out_idx, 4)))
+template <class T, class P>
+int compact_run(ki_ctx* ctx, const void* d_x, size_t n, const void* h_thr, void* d_out_vals, int32_t* d_out_idx,
+                int64_t index_base, uint64_t* d_count, cudaStream_t s) {
+    constexpr int kTile = CShape<T>::kTile;
+    if (n > 0 && !ki::aligned(d_x, sizeof(T))) return ki::set_error(ctx, KI_ERR_ARG, "compact: misaligned input");
+    if ((d_out_vals && !ki::aligned(d_out_vals, sizeof(T))) || (d_out_idx && !ki::aligned(d_out_idx, 4)))
         return ki::set_error(ctx, KI_ERR_ARG, "compact: misaligned output");
-    if (index_base < INT32_MIN || (n > 0 && index_base + (int64_t)n - 1 > (int64_t)INT32_MAX))
-        return ki::set_error(ctx, KI_ERR_ARG, "compact: indices do not fit Int32");
-    KI_GUARD(ctx);
-    cudaStream_t s = ki::as_stream(stream);
     if (n == 0) {
         if (d_count) KI_CUDA(ctx, cudaMemsetAsync(d_count, 0, sizeof(uint64_t), s));
         return KI_OK;
@@ -283,7 +313,8 @@ extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float 
     CompactArgs a;
     a.x = d_x;
     a.n = n;
-    a.thr = threshold;
+    a.thr_bits = 0;
+    memcpy(&a.thr_bits, h_thr, sizeof(T));
     a.out_vals = d_out_vals;
     a.out_idx = d_out_idx;
     a.index_base = index_base;
@@ -297,8 +328,60 @@ extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float 
     a.tma_in = ki::aligned(d_x, 16);
     size_t grid = (size_t)ctx->sm_count * kCtasPerSm;
     if (grid > ntiles) grid = ntiles;
-    if (d_out_vals && d_out_idx) return launch_compact<true, true>(ctx, a, grid, s);
-    if (d_out_vals) return launch_compact<true, false>(ctx, a, grid, s);
-    if (d_out_idx) return launch_compact<false, true>(ctx, a, grid, s);
-    return launch_compact<false, false>(ctx, a, grid, s);
+    if (d_out_vals && d_out_idx) return launch_compact<T, P, true, true>(ctx, a, grid, s);
+    if (d_out_vals) return launch_compact<T, P, true, false>(ctx, a, grid, s);
+    if (d_out_idx) return launch_compact<T, P, false, true>(ctx, a, grid, s);
+    return launch_compact<T, P, false, false>(ctx, a, grid, s);
+}
+
+template <class T>
+int compact_pred(ki_ctx* ctx, int pred, const void* d_x, size_t n, const void* h_thr, void* d_out_vals,
+                 int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, cudaStream_t s) {
+    switch (pred) {
+        case KI_PRED_GT: return compact_run<T, PGt>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_PRED_GE: return compact_run<T, PGe>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_PRED_LT: return compact_run<T, PLt>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_PRED_LE: return compact_run<T, PLe>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_PRED_EQ: return compact_run<T, PEq>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_PRED_NE: return compact_run<T, PNe>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        default: return ki::set_error(ctx, KI_ERR_ARG, "compact: unknown predicate");
+    }
+}
+
+int check_common(ki_ctx* ctx, const void* d_x, size_t n, int64_t index_base) {
+    if (n > 0 && !d_x) return ki::set_error(ctx, KI_ERR_ARG, "compact: null input");
+    if (index_base < INT32_MIN || (n > 0 && index_base + (int64_t)n - 1 > (int64_t)INT32_MAX))
+        return ki::set_error(ctx, KI_ERR_ARG, "compact: indices do not fit Int32");
+    return KI_OK;
+}
+
+}  // namespace
+
+extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float threshold, float* d_out_vals,
+                                 int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream) {
+    KI_CHECK_CTX(ctx);
+    int rc = check_common(ctx, d_x, n, index_base);
+    if (rc) return rc;
+    KI_GUARD(ctx);
+    return compact_run<float, PGt>(ctx, d_x, n, &threshold, d_out_vals, d_out_idx, index_base, d_count,
+                                   ki::as_stream(stream));
+}
+
+extern "C" int ki_compact(ki_ctx* ctx, int pred, int dtype, const void* d_x, size_t n, const void* h_thr,
+                          void* d_out_vals, int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream) {
+    KI_CHECK_CTX(ctx);
+    if (!h_thr) return ki::set_error(ctx, KI_ERR_ARG, "compact: null threshold");
+    int rc = check_common(ctx, d_x, n, index_base);
+    if (rc) return rc;
+    KI_GUARD(ctx);
+    cudaStream_t s = ki::as_stream(stream);
+    switch (dtype) {
+        case KI_I32: return compact_pred<int32_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_U32: return compact_pred<uint32_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_I64: return compact_pred<int64_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_U64: return compact_pred<uint64_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_F32: return compact_pred<float>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        case KI_F64: return compact_pred<double>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+        default: return ki::set_error(ctx, KI_ERR_ARG, "compact: dtype must be Int32/UInt32/Int64/UInt64/Float32/Float64");
+    }
 }

@@ -30,7 +30,7 @@ __all__ = [
     "Up", "Down", "Xor", "Idx", "All", "AnyLane", "Uni", "Ballot", "KIError", "KIArgumentError",
     "KITimeoutError", "Context", "context", "warpsize", "get_warpsize", "devices", "shfl", "warpreduce",
     "warpfold", "vote", "vload", "vstore", "vload_multi", "vstore_multi", "generate_partN", "access",
-    "message_pass", "vcopy", "vcopy_host", "reduce", "reduce_rows", "scan", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
+    "message_pass", "vcopy", "vcopy_host", "reduce", "reduce_rows", "scan", "compact", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
     "fp8_gemm", "fill_uniform", "fill_int_range", "fill_bytes", "fill_normal", "fill_e4m3_uniform",
 ]
 
@@ -538,6 +538,37 @@ def scan(x, op: str = "+", exclusive: bool = False, init=None, out=None, stream=
     context(d).call("ki_scan", _GENERIC_OPS[op], _dtype_code(x), int(bool(exclusive)), _ptr(x), _ptr(out), x.numel(),
                     ctypes.c_void_p(init_buf.ctypes.data) if init_buf is not None else None, _stream_ptr(stream, d))
     return out
+
+
+_PREDS = {">": 0, ">=": 1, "<": 2, "<=": 3, "==": 4, "!=": 5}
+
+
+def compact(x, pred: str, threshold, out_vals=None, out_idx=None, count=None, index_base: int = 1, stream=None,
+            trim: bool = True):
+    """filter(v -> v pred threshold, x) and findall for Int32/UInt32/Int64/UInt64/Float32/Float64 ``x``
+    (IEEE comparisons).  Returns (vals, idx, count) like ``vote_compact``."""
+    import numpy as np
+
+    torch = _torch()
+    d = _dev(x)
+    if pred not in _PREDS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"compact: pred must be one of {sorted(_PREDS)}")
+    x = x.contiguous()
+    n = x.numel()
+    np_dt = {torch.int32: np.int32, torch.uint32: np.uint32, torch.int64: np.int64, torch.uint64: np.uint64,
+             torch.float32: np.float32, torch.float64: np.float64}.get(x.dtype)
+    if np_dt is None:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"compact: unsupported dtype {x.dtype}")
+    thr = np.array([threshold], dtype=np_dt)
+    out_vals = torch.empty(n, dtype=x.dtype, device=x.device) if out_vals is None else out_vals
+    out_idx = torch.empty(n, dtype=torch.int32, device=x.device) if out_idx is None else out_idx
+    count = torch.zeros((), dtype=torch.uint64, device=x.device) if count is None else count
+    context(d).call("ki_compact", _PREDS[pred], _dtype_code(x), _ptr(x), n, ctypes.c_void_p(thr.ctypes.data),
+                    _ptr(out_vals), _ptr(out_idx), ctypes.c_int64(int(index_base)), _ptr(count), _stream_ptr(stream, d))
+    if trim:
+        k = int(count.item())
+        return out_vals[:k], out_idx[:k], count
+    return out_vals, out_idx, count
 
 
 def vote_compact(x, threshold: float, out_vals=None, out_idx=None, count=None, index_base: int = 1,

@@ -45,6 +45,7 @@ SIGNATURES = {
     "ki_reduce_sum_i64": (_i32, [_vp, _vp, _sz, _vp, _vp]),
     "ki_scan_inclusive_i64": (_i32, [_vp, _vp, _vp, _sz, _i64, _vp]),
     "ki_reduce": (_i32, [_vp, _i32, _i32, _vp, _sz, _vp, _vp]),
+    "ki_compact": (_i32, [_vp, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _i64, _vp, _vp]),
     "ki_reduce_rows": (_i32, [_vp, _i32, _i32, _vp, _sz, _sz, _sz, _vp, _vp]),
     "ki_scan": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _sz, _vp, _vp]),
     "ki_scan_inclusive_i64_noalloc": (_i32, [_vp, _vp, _sz, _i64, _vp]),

@@ -132,3 +132,34 @@ def test_normal_generator_distribution(KI, dev):
     assert abs(zd.mean().item()) < 2e-3 and abs(zd.std().item() - 1) < 2e-3
     assert abs((z > 0.5).double().mean().item() - 0.308538) < 1e-3
     assert torch.isfinite(z).all()
+
+
+PRED_FN = {">": np.greater, ">=": np.greater_equal, "<": np.less, "<=": np.less_equal, "==": np.equal,
+           "!=": np.not_equal}
+
+
+@pytest.mark.parametrize("dt", [np.int32, np.uint32, np.int64, np.uint64, np.float32, np.float64],
+                         ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("pred", list(PRED_FN))
+def test_compact_generic_vs_oracle(KI, dev, dt, pred):
+    """ki_compact: every predicate and element type; sizes across tile boundaries (8192 / 16384
+    elements), an unaligned start, NaN for floats; bit-exact against numpy's IEEE comparisons."""
+    import torch
+
+    rng = np.random.default_rng(17)
+    for n, off in [(1, 0), (100, 1), (8191, 0), (8193, 1), (16385, 0), (3 * 16384 + 77, 1), ((1 << 20) + 13, 0)]:
+        if np.dtype(dt).kind == "f":
+            base = rng.integers(-8, 8, n + off).astype(dt) * np.asarray(0.5, dtype=dt)
+            base[rng.integers(0, n + off, 5)] = np.nan
+            thr = np.asarray(1.5, dtype=dt)
+        else:
+            base = rng.integers(0 if np.dtype(dt).kind == "u" else -8, 8, n + off).astype(dt)
+            thr = np.asarray(3, dtype=dt)
+        x = base[off:]
+        xd = torch.from_numpy(base).to(dev)[off:]
+        vals, idx, cnt = KI.compact(xd, pred, thr.item(), index_base=1)
+        keep = np.nonzero(PRED_FN[pred](x, thr))[0]
+        assert cnt.item() == keep.size, (n, off)
+        assert np.array_equal(idx.cpu().numpy(), (keep + 1).astype(np.int32)), (n, off)
+        assert np.array_equal(vals.cpu().numpy().view(np.uint8), x[keep].view(np.uint8)), (n, off)
+    KI.context(0).check()

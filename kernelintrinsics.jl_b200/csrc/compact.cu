@@ -27,9 +27,12 @@
 // Measured at n = 2^28 (0.467 ms, 0.57 of the copy peak): without the stores the same kernel takes
 // 0.235 ms.  Writing the output streams evicts tiles that wait for their prefix, so most second-pass
 // reads come back from DRAM; the prefetch turns them into one asynchronous bulk read per tile
-// (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read, tiles
-// kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-element tiles, one or
-// two CTAs per SM with more warps, looking tile k up right after its count, early tickets.
+// (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read (also
+// with the lines demoted to normal priority after the second read: 0.48 ms), evict-first second
+// reads (0.50), tiles kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-
+// element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
+// per SM of 16 warps over 64 KiB tiles (0.48), looking tile k up right after its count, early
+// tickets.  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/lookback.cuh"
@@ -40,15 +43,24 @@ namespace {
 #ifndef KI_COMPACT_LOOKBACK_K
 #define KI_COMPACT_LOOKBACK_K 1
 #endif
+#ifndef KI_COMPACT_PREFETCH
+#define KI_COMPACT_PREFETCH 1
+#endif
 #ifndef KI_COMPACT_CTAS_PER_SM
 #define KI_COMPACT_CTAS_PER_SM 3
 #endif
-constexpr int kWorkWarps = 8;
+#ifndef KI_COMPACT_WORK_WARPS
+#define KI_COMPACT_WORK_WARPS 8
+#endif
+#ifndef KI_COMPACT_ROWS
+#define KI_COMPACT_ROWS 16
+#endif
+constexpr int kWorkWarps = KI_COMPACT_WORK_WARPS;
 constexpr int kLookWarp = kWorkWarps;
 constexpr int kWorkThreads = 32 * kWorkWarps;
 constexpr int kThreads = kWorkThreads + 32;
-constexpr size_t kTileBytes = 65536;  // 16384 elements of 4 bytes or 8192 of 8
-constexpr int kRows = 16;             // rows of 32 lanes x one 16-byte vector per work warp
+constexpr int kRows = KI_COMPACT_ROWS;  // rows of 32 lanes x one 16-byte vector per work warp
+constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 512;  // 64 KiB: 16384 elements of 4 bytes or 8192 of 8
 constexpr int kBatch = 8;             // rows loaded at once in the second pass
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
@@ -149,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
             if (have_old) {
                 Pending& o = slot[cur ^ 1];
                 // bring tile k-1 back into L2 (if it left) while its prefix is looked up
-                if (lane == 0 && bulk_ok(o.t)) ki::bulk_prefetch_l2(x + o.t * kTile, (uint32_t)kTileBytes);
+                if (KI_COMPACT_PREFETCH && lane == 0 && bulk_ok(o.t))
+                    ki::bulk_prefetch_l2(x + o.t * kTile, (uint32_t)kTileBytes);
                 const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, 0, a.status, a.timeout_ns);
                 if (lane == 0) o.tile_excl = ex;
             }

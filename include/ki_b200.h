@@ -61,12 +61,14 @@ typedef enum {
 typedef enum { KI_SHFL_UP = 0, KI_SHFL_DOWN = 1, KI_SHFL_XOR = 2, KI_SHFL_IDX = 3 } ki_dir;
 typedef enum { KI_VOTE_ALL = 0, KI_VOTE_ANY = 1, KI_VOTE_UNI = 2, KI_VOTE_BALLOT = 3 } ki_mode;
 
-/* Element types and binary operators for the warp-level entry points. */
+/* Element types and binary operators (warp-level and device-wide entry points). */
 typedef enum {
     KI_I8 = 0, KI_U8 = 1, KI_I16 = 2, KI_U16 = 3, KI_I32 = 4, KI_U32 = 5,
     KI_I64 = 6, KI_U64 = 7, KI_F32 = 8, KI_F64 = 9
 } ki_dtype;
-typedef enum { KI_OP_ADD = 0, KI_OP_MAX = 1, KI_OP_MIN = 2, KI_OP_OR = 3, KI_OP_AND = 4, KI_OP_XOR = 5 } ki_op;
+typedef enum {
+    KI_OP_ADD = 0, KI_OP_MAX = 1, KI_OP_MIN = 2, KI_OP_OR = 3, KI_OP_AND = 4, KI_OP_XOR = 5, KI_OP_MUL = 6
+} ki_op;
 
 /* ---- library / context ------------------------------------------------------------------- */
 
@@ -101,6 +103,20 @@ int ki_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* strea
  * re-entrant on one context: two calls in flight on different streams share the staging slots. */
 int ki_vcopy_host(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* stream);
 
+/* ---- strided copies: copyto! between strided views ------------------------------------------
+ * Replaces: the AbstractArray fallbacks of vload / vstore! (src/vectorization.jl:202-211, 290-297;
+ * _vload_batch / _vstore_batch!, :426-448), which move a strided view element by element.
+ * ki_vcopy_2d: height rows of width bytes; row r goes from src + r*spitch to dst + r*dpitch (bytes).
+ * Any byte alignment and any pitch >= width (a block of a column-major array: one row per column).
+ * The two ranges must not overlap (KI_ERR_ARG).  width or height 0: nothing to do. */
+int ki_vcopy_2d(ki_ctx* ctx, void* dst, size_t dpitch, const void* src, size_t spitch, size_t width_bytes,
+                size_t height, void* stream);
+/* ki_vcopy_strided: dst[i*dst_stride] = src[i*src_stride] for i < count, elements of elem_bytes
+ * (1, 2, 4, 8 or 16) with strides in elements of either sign (view(x, n:-2:1)); both pointers aligned
+ * to the element size; src_stride 0 broadcasts one element; the ranges must not overlap. */
+int ki_vcopy_strided(ki_ctx* ctx, void* dst, int64_t dst_stride, const void* src, int64_t src_stride,
+                     size_t elem_bytes, size_t count, void* stream);
+
 /* ---- (a3) grid-wide reduce (@warpfold, src/warp.jl:273-282) ---------------------------------
  * sum(x) of n Float32 values, accumulated in Float64 across threads; writes the Float32 result to
  * d_out_f32 and/or the Float64 result to d_out_f64 (either may be NULL, not both).  n == 0 gives 0.
@@ -110,18 +126,20 @@ int ki_reduce_sum_f32(ki_ctx* ctx, const float* d_x, size_t n, float* d_out_f32,
 /* sum of Int64 with two's-complement wrap-around (the shard total of the sharded scan). */
 int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out, void* stream);
 /* Device-wide reduce for any of the reference's fold operators that Base names (@warpfold takes any
- * op, src/warp.jl:273-282; the device-wide result is Base.sum / maximum / minimum).
- * op: KI_OP_ADD, KI_OP_MAX or KI_OP_MIN; dtype: KI_I32, KI_U32, KI_I64, KI_U64, KI_F32, KI_F64.
- * d_out receives one value of the result type: for KI_OP_ADD Int32 -> Int64 and UInt32 -> UInt64
- * (Base.add_sum widens), Int64/UInt64 wrap, Float32 stays Float32 (accumulated in Float64),
- * Float64 stays Float64; for KI_OP_MAX / KI_OP_MIN the input type (NaN propagates, +0.0 > -0.0,
- * as Base.max / Base.min).  n = 0: KI_OP_ADD writes zero, KI_OP_MAX / KI_OP_MIN return KI_ERR_ARG
- * (Base throws on an empty maximum).  Deterministic for a given n and device. */
+ * op, src/warp.jl:273-282; the device-wide result is Base.sum / prod / maximum / minimum /
+ * reduce(|, &, xor)).  op: KI_OP_ADD, KI_OP_MUL, KI_OP_MAX, KI_OP_MIN, KI_OP_OR, KI_OP_AND, KI_OP_XOR;
+ * dtype: KI_I8 ... KI_U64, KI_F32, KI_F64 (the bitwise operators take integers only).
+ * d_out receives one value of the result type: for KI_OP_ADD and KI_OP_MUL integers narrower than
+ * 64 bits widen to Int64 / UInt64 (Base.add_sum, Base.mul_prod), 64-bit integers wrap, Float32 stays
+ * Float32 (accumulated in Float64), Float64 stays Float64; for the other operators the input type
+ * (KI_OP_MAX / KI_OP_MIN: NaN propagates, +0.0 > -0.0, as Base.max / Base.min).  n = 0: KI_OP_ADD
+ * writes zero, KI_OP_MUL one, the others return KI_ERR_ARG (Base throws on an empty maximum).
+ * Deterministic for a given n and device. */
 int ki_reduce(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t n, void* d_out, void* stream);
 /* Segmented reduce: one ki_reduce per row of a row-major rows x cols matrix whose rows start ld
  * elements apart (ld >= cols; a column-major Julia matrix reduced along dims=1 has rows = its
  * columns).  d_out receives rows values of ki_reduce's result type.  cols = 0: KI_OP_ADD writes
- * zeros, KI_OP_MAX / KI_OP_MIN return KI_ERR_ARG.  Deterministic for a given shape and device. */
+ * zeros, KI_OP_MUL ones, the others return KI_ERR_ARG.  Deterministic for a given shape and device. */
 int ki_reduce_rows(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t rows, size_t cols, size_t ld,
                    void* d_out, void* stream);
 
@@ -138,9 +156,11 @@ int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size
  * op, dtype and the result type as for ki_reduce; d_out holds n values of the result type.
  * exclusive = 0: out[i] = op(init, in[0], ..., in[i]); exclusive != 0: out[i] = op(init, in[0], ...,
  * in[i-1]), out[0] = init.  h_init: host pointer to one value of the result type, or NULL for the
- * operator's identity (0, the lowest value, the highest value).  in == out is allowed when the input
+ * operator's identity (0 for + | xor, 1 for *, all ones for &, the lowest value for max, the highest
+ * for min).  in == out is allowed when the input
  * and result types have the same size; other overlaps return KI_ERR_ARG.  Float sums accumulate in
- * Float64 (within 1e-5*log2(n) of a Float64 scan).  Int64 + with a seed is ki_scan_inclusive_i64. */
+ * Float64 (within 1e-5*log2(n) of a Float64 scan), Float32 products too.  Int64 + with a seed is
+ * ki_scan_inclusive_i64. */
 int ki_scan(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in, void* d_out, size_t n,
             const void* h_init, void* stream);
 

@@ -11,6 +11,7 @@
 //
 // Reads of the aligned source words never leave the 16-byte words that hold source bytes, so they
 // stay inside the source allocation's pages.  Head and tail bytes are copied by block 0, warp 0.
+#include "ki/bytes.cuh"
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 
@@ -34,26 +35,6 @@ namespace {
 constexpr int kThreads = KI_COPY_THREADS;
 constexpr int kUnroll = KI_COPY_UNROLL;  // 32-chunk rows per warp span
 constexpr int kSpan = 32 * kUnroll;      // 16-byte chunks per warp span
-
-template <int WS>
-__device__ __forceinline__ uint4 realign(const uint4& lo, const uint4& hi, unsigned sh) {
-    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    uint4 r;
-    r.x = __funnelshift_r(w[WS + 0], w[WS + 1], sh);
-    r.y = __funnelshift_r(w[WS + 1], w[WS + 2], sh);
-    r.z = __funnelshift_r(w[WS + 2], w[WS + 3], sh);
-    r.w = __funnelshift_r(w[WS + 3], w[WS + 4], sh);
-    return r;
-}
-
-__device__ __forceinline__ uint4 shfl_down_u4(const uint4& v) {
-    uint4 r;
-    r.x = __shfl_down_sync(0xffffffffu, v.x, 1);
-    r.y = __shfl_down_sync(0xffffffffu, v.y, 1);
-    r.z = __shfl_down_sync(0xffffffffu, v.z, 1);
-    r.w = __shfl_down_sync(0xffffffffu, v.w, 1);
-    return r;
-}
 
 struct CopyArgs {
     uint8_t* dst;          // start of the whole destination range
@@ -109,9 +90,9 @@ __global__ void __launch_bounds__(kThreads, KI_COPY_MIN_BLOCKS) vcopy_kernel(Cop
 #pragma unroll
             for (int j = 0; j < kUnroll; ++j) {
                 const size_t k = base + 32 * j;
-                uint4 hi = shfl_down_u4(lo[j]);
+                uint4 hi = ki::shfl_down_u4(lo[j]);
                 if (lane == 31) hi = ex[j];
-                if (k < nc) d[k] = realign<WS>(lo[j], hi, a.sh);
+                if (k < nc) d[k] = ki::realign<WS>(lo[j], hi, a.sh);
             }
         }
     }

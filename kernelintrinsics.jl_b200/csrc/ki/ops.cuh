@@ -5,6 +5,11 @@
 //        back to Float32 once at the end (Base keeps Float32, within the documented tolerance).
 //   Max  maximum / accumulate(max): a NaN operand wins, +0.0 is larger than -0.0 (Base.max).
 //   Min  minimum / accumulate(min): a NaN operand wins, -0.0 is smaller than +0.0 (Base.min).
+//   Mul  prod / cumprod: integers wrap; small integers widen as Base.mul_prod does (Int8/Int16/
+//        Int32 -> Int64, UInt8/UInt16/UInt32 -> UInt64); Float32 multiplies in Float64 and is
+//        rounded back to Float32 at the output.
+//   Or, And, Xor  reduce(|, x) / accumulate(&, x) / xor over integers, in the input type.
+// Sums widen Int8/Int16 and UInt8/UInt16 as Int32/UInt32 do (Base.add_sum).
 //
 // Traits<T, Op> gives the accumulation type A, the result type R, lift (T -> A), lower (A -> R),
 // the identity of A and the operator on A.
@@ -15,11 +20,23 @@
 #include <cstring>
 #include <type_traits>
 
+#include "../../../include/ki_b200.h"
+
 namespace ki {
 
 struct JAdd {};
 struct JMax {};
 struct JMin {};
+struct JMul {};
+struct JOr {};
+struct JAnd {};
+struct JXor {};
+
+template <class Op>
+struct IsBitwise : std::false_type {};
+template <> struct IsBitwise<JOr> : std::true_type {};
+template <> struct IsBitwise<JAnd> : std::true_type {};
+template <> struct IsBitwise<JXor> : std::true_type {};
 
 template <class T>
 __device__ __forceinline__ T jadd(T a, T b) {
@@ -74,6 +91,49 @@ struct Traits<T, JAdd> {
     __device__ static __forceinline__ A identity() { return A(0); }
     __device__ static __forceinline__ A op(A a, A b) { return jadd(a, b); }
 };
+
+template <class T>
+__device__ __forceinline__ T jmul(T a, T b) {
+    if constexpr (std::is_integral<T>::value) {
+        using U = typename std::make_unsigned<T>::type;
+        return (T)((U)a * (U)b);
+    } else {
+        return a * b;
+    }
+}
+
+// Mul: the accumulation and result types of Add
+template <class T>
+struct Traits<T, JMul> {
+    using A = typename Traits<T, JAdd>::A;
+    using R = typename Traits<T, JAdd>::R;
+    __host__ __device__ static __forceinline__ A lift(T x) { return (A)x; }
+    __host__ __device__ static __forceinline__ R lower(A a) { return (R)a; }
+    __device__ static __forceinline__ A identity() { return A(1); }
+    __device__ static __forceinline__ A op(A a, A b) { return jmul(a, b); }
+};
+
+// Or / And / Xor: integers only, in the input type
+template <class T, class Op>
+struct BitTraits {
+    static_assert(std::is_integral<T>::value, "bitwise operators take integers");
+    using A = T;
+    using R = T;
+    __host__ __device__ static __forceinline__ A lift(T x) { return x; }
+    __host__ __device__ static __forceinline__ R lower(A a) { return a; }
+    __host__ __device__ static __forceinline__ A identity() { return std::is_same<Op, JAnd>::value ? (A)~A(0) : A(0); }
+    __device__ static __forceinline__ A op(A a, A b) {
+        if constexpr (std::is_same<Op, JOr>::value) return a | b;
+        else if constexpr (std::is_same<Op, JAnd>::value) return a & b;
+        else return a ^ b;
+    }
+};
+template <class T>
+struct Traits<T, JOr> : BitTraits<T, JOr> {};
+template <class T>
+struct Traits<T, JAnd> : BitTraits<T, JAnd> {};
+template <class T>
+struct Traits<T, JXor> : BitTraits<T, JXor> {};
 
 template <class T>
 __device__ __forceinline__ T lowest_of() {
@@ -145,10 +205,93 @@ struct OpFn {
     __device__ __forceinline__ A operator()(A a, A b) const { return Traits<T, Op>::op(a, b); }
 };
 
+// The identity of Op as an element of T (what pads a partial tile).
+template <class T, class Op>
+__device__ __forceinline__ T pad_value() {
+    if constexpr (std::is_same<Op, JAdd>::value || std::is_same<Op, JOr>::value || std::is_same<Op, JXor>::value)
+        return T(0);
+    else if constexpr (std::is_same<Op, JMul>::value) return T(1);
+    else if constexpr (std::is_same<Op, JAnd>::value) return (T)~T(0);
+    else if constexpr (std::is_same<Op, JMax>::value) return lowest_of<T>();
+    else return highest_of<T>();
+}
+
+// Calls f(T{}) for the element type an ABI dtype code names (KI_I8 ... KI_F64); bad for another code.
+template <class F>
+inline int with_dtype(int dtype, int bad, F&& f) {
+    switch (dtype) {
+        case KI_I8: return f(int8_t{});
+        case KI_U8: return f(uint8_t{});
+        case KI_I16: return f(int16_t{});
+        case KI_U16: return f(uint16_t{});
+        case KI_I32: return f(int32_t{});
+        case KI_U32: return f(uint32_t{});
+        case KI_I64: return f(int64_t{});
+        case KI_U64: return f(uint64_t{});
+        case KI_F32: return f(float{});
+        case KI_F64: return f(double{});
+        default: return bad;
+    }
+}
+
+// Whether Op is defined on T (the bitwise operators take integers only).
+template <class T, class Op>
+constexpr bool op_takes() {
+    return std::is_integral<T>::value || !IsBitwise<Op>::value;
+}
+
 // 16-byte vector of T.
 template <class T>
 struct alignas(16) Vec16 {
     T v[16 / sizeof(T)];
+};
+
+// 16 bytes of T kept as four 32-bit words, elements taken out on use.  An array of sixteen 1-byte
+// elements would occupy sixteen registers; this keeps four whatever the element size.
+template <class T>
+struct Packed16 {
+    uint4 raw;
+    static constexpr int kN = (int)(16 / sizeof(T));
+    __device__ __forceinline__ uint32_t word(int k) const { return k == 0 ? raw.x : k == 1 ? raw.y : k == 2 ? raw.z : raw.w; }
+    __device__ __forceinline__ void set_word(int k, uint32_t v) {
+        if (k == 0) raw.x = v;
+        else if (k == 1) raw.y = v;
+        else if (k == 2) raw.z = v;
+        else raw.w = v;
+    }
+    __device__ __forceinline__ T get(int e) const {
+        T x;
+        if constexpr (sizeof(T) == 8) {
+            const uint64_t b = ((uint64_t)word(2 * e + 1) << 32) | word(2 * e);
+            memcpy(&x, &b, 8);
+        } else if constexpr (sizeof(T) == 4) {
+            const uint32_t b = word(e);
+            memcpy(&x, &b, 4);
+        } else {
+            using U = typename std::make_unsigned<T>::type;
+            constexpr int kPerWord = (int)(4 / sizeof(T));
+            x = (T)(U)(word(e / kPerWord) >> (8 * sizeof(T) * (e % kPerWord)));
+        }
+        return x;
+    }
+    __device__ __forceinline__ void set(int e, T x) {
+        if constexpr (sizeof(T) == 8) {
+            uint64_t b;
+            memcpy(&b, &x, 8);
+            set_word(2 * e, (uint32_t)b);
+            set_word(2 * e + 1, (uint32_t)(b >> 32));
+        } else if constexpr (sizeof(T) == 4) {
+            uint32_t b;
+            memcpy(&b, &x, 4);
+            set_word(e, b);
+        } else {
+            using U = typename std::make_unsigned<T>::type;
+            constexpr int kPerWord = (int)(4 / sizeof(T));
+            const int sh = 8 * (int)sizeof(T) * (e % kPerWord);
+            const uint32_t m = (uint32_t)(U)~U(0) << sh;
+            set_word(e / kPerWord, (word(e / kPerWord) & ~m) | (((uint32_t)(U)x << sh) & m));
+        }
+    }
 };
 
 }  // namespace ki

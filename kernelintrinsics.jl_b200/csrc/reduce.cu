@@ -1,4 +1,5 @@
-// reduce.cu -- grid-wide reduce (Base.sum / maximum / minimum) built from @warpfold-style folds.
+// reduce.cu -- grid-wide reduce (Base.sum / prod / maximum / minimum / reduce(|, &, xor)) built from
+// @warpfold-style folds.
 //
 // One launch: every thread streams 16-byte vectors (several loads in flight), folds them into a
 // per-thread accumulator, the warp folds with __shfl_xor_sync (every lane holds the warp total;
@@ -9,8 +10,9 @@
 //
 // Operators and types follow Julia Base (ki/ops.cuh): Float32 sums accumulate in Float64 once each
 // 16-byte vector has been added in Float32 (within a few ulps of a Float64 sum; the parity bound is
-// 1e-5*log2(n) relative), Int32/UInt32 sums widen to 64 bits, Int64 sums wrap, and maximum/minimum
-// propagate NaN and order signed zeros as Base.max/Base.min do.
+// 1e-5*log2(n) relative), sums and products of integers narrower than 64 bits widen to 64 bits,
+// 64-bit ones wrap, maximum/minimum propagate NaN and order signed zeros as Base.max/Base.min do,
+// and the bitwise operators take integers in their own type.
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 #include "ki/ops.cuh"
@@ -34,16 +36,16 @@ constexpr int kBlocksPerSm = KI_REDUCE_BLOCKS_PER_SM;
 // Fold of one 16-byte vector into the accumulation type.  Float32 sums add the four lanes in
 // Float32 first (one rounding per vector), everything else folds in the accumulation type.
 template <class T, class Op>
-__device__ __forceinline__ typename ki::Traits<T, Op>::A fold_vec(const ki::Vec16<T>& v) {
+__device__ __forceinline__ typename ki::Traits<T, Op>::A fold_vec(const ki::Packed16<T>& v) {
     using Tr = ki::Traits<T, Op>;
     using A = typename Tr::A;
     constexpr int kV = (int)(16 / sizeof(T));
     if constexpr (std::is_same<T, float>::value && std::is_same<Op, ki::JAdd>::value) {
-        return (double)((v.v[0] + v.v[1]) + (v.v[2] + v.v[3]));
+        return (double)((v.get(0) + v.get(1)) + (v.get(2) + v.get(3)));
     } else {
-        A r = Tr::lift(v.v[0]);
+        A r = Tr::lift(v.get(0));
 #pragma unroll
-        for (int i = 1; i < kV; ++i) r = Tr::op(r, Tr::lift(v.v[i]));
+        for (int i = 1; i < kV; ++i) r = Tr::op(r, Tr::lift(v.get(i)));
         return r;
     }
 }
@@ -68,14 +70,14 @@ __global__ void __launch_bounds__(kThreads)
                   unsigned int* ticket, typename ki::Traits<T, Op>::R* out, typename ki::Traits<T, Op>::A* out_acc) {
     using Tr = ki::Traits<T, Op>;
     using A = typename Tr::A;
-    using V = ki::Vec16<T>;
+    using V = ki::Packed16<T>;
     constexpr int kVec = (int)(16 / sizeof(T));
     const ki::OpFn<T, Op> f;
     const A id = Tr::identity();
     __shared__ A sm[kWarps];
     __shared__ int is_last;
 
-    const V* xv = reinterpret_cast<const V*>(x + head);
+    const uint4* xv = reinterpret_cast<const uint4*>(x + head);
     const size_t stride = (size_t)gridDim.x * kThreads;
     size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x;
     A acc = id;
@@ -83,15 +85,15 @@ __global__ void __launch_bounds__(kThreads)
         V v[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(xv + i + u * stride));
-            v[u] = *reinterpret_cast<const V*>(&raw);
+            v[u].raw = __ldcs(xv + i + u * stride);
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) acc = Tr::op(acc, fold_vec<T, Op>(v[u]));
     }
     for (; i < nvec; i += stride) {
-        const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(xv + i));
-        acc = Tr::op(acc, fold_vec<T, Op>(*reinterpret_cast<const V*>(&raw)));
+        V v;
+        v.raw = __ldcs(xv + i);
+        acc = Tr::op(acc, fold_vec<T, Op>(v));
     }
     // unaligned head and the tail that does not fill a vector
     if (blockIdx.x == 0) {
@@ -149,28 +151,22 @@ int reduce_generic(ki_ctx* ctx, const void* d_x, size_t n, void* d_out, cudaStre
     using R = typename ki::Traits<T, Op>::R;
     if (n > 0 && !ki::aligned(d_x, sizeof(T))) return ki::set_error(ctx, KI_ERR_ARG, "reduce: misaligned input");
     if (!ki::aligned(d_out, sizeof(R))) return ki::set_error(ctx, KI_ERR_ARG, "reduce: misaligned output");
-    if (n == 0) {
-        if constexpr (!std::is_same<Op, ki::JAdd>::value) {
-            return ki::set_error(ctx, KI_ERR_ARG, "reduce: maximum/minimum over an empty collection");
-        } else {
-            KI_CUDA(ctx, cudaMemsetAsync(d_out, 0, sizeof(R), s));
-            return KI_OK;
-        }
-    }
+    // n = 0: + and * give their identity (the kernel reads nothing); the others have none (Base throws)
+    if (n == 0 && !std::is_same<Op, ki::JAdd>::value && !std::is_same<Op, ki::JMul>::value)
+        return ki::set_error(ctx, KI_ERR_ARG, "reduce: reducing an empty collection with an operator that has no identity");
     return launch_reduce<T, Op>(ctx, static_cast<const T*>(d_x), n, static_cast<R*>(d_out), nullptr, s);
 }
 
 template <class Op>
 int reduce_dtype(ki_ctx* ctx, int dtype, const void* d_x, size_t n, void* d_out, cudaStream_t s) {
-    switch (dtype) {
-        case KI_I32: return reduce_generic<int32_t, Op>(ctx, d_x, n, d_out, s);
-        case KI_U32: return reduce_generic<uint32_t, Op>(ctx, d_x, n, d_out, s);
-        case KI_I64: return reduce_generic<int64_t, Op>(ctx, d_x, n, d_out, s);
-        case KI_U64: return reduce_generic<uint64_t, Op>(ctx, d_x, n, d_out, s);
-        case KI_F32: return reduce_generic<float, Op>(ctx, d_x, n, d_out, s);
-        case KI_F64: return reduce_generic<double, Op>(ctx, d_x, n, d_out, s);
-        default: return ki::set_error(ctx, KI_ERR_ARG, "reduce: dtype must be Int32/UInt32/Int64/UInt64/Float32/Float64");
-    }
+    constexpr int kBad = -1000;
+    const int rc = ki::with_dtype(dtype, kBad, [&](auto tag) -> int {
+        using T = decltype(tag);
+        if constexpr (ki::op_takes<T, Op>()) return reduce_generic<T, Op>(ctx, d_x, n, d_out, s);
+        else return kBad;
+    });
+    if (rc == kBad) return ki::set_error(ctx, KI_ERR_ARG, "reduce: the operator does not take this element type");
+    return rc;
 }
 
 }  // namespace
@@ -215,6 +211,10 @@ extern "C" int ki_reduce(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t
         case KI_OP_ADD: return reduce_dtype<ki::JAdd>(ctx, dtype, d_x, n, d_out, s);
         case KI_OP_MAX: return reduce_dtype<ki::JMax>(ctx, dtype, d_x, n, d_out, s);
         case KI_OP_MIN: return reduce_dtype<ki::JMin>(ctx, dtype, d_x, n, d_out, s);
-        default: return ki::set_error(ctx, KI_ERR_ARG, "reduce: op must be KI_OP_ADD, KI_OP_MAX or KI_OP_MIN");
+        case KI_OP_MUL: return reduce_dtype<ki::JMul>(ctx, dtype, d_x, n, d_out, s);
+        case KI_OP_OR: return reduce_dtype<ki::JOr>(ctx, dtype, d_x, n, d_out, s);
+        case KI_OP_AND: return reduce_dtype<ki::JAnd>(ctx, dtype, d_x, n, d_out, s);
+        case KI_OP_XOR: return reduce_dtype<ki::JXor>(ctx, dtype, d_x, n, d_out, s);
+        default: return ki::set_error(ctx, KI_ERR_ARG, "reduce: unknown operator");
     }
 }

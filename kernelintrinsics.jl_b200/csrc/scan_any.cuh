@@ -1,0 +1,344 @@
+// scan_any.cuh -- device-wide inclusive or exclusive scan for Base's +, *, max, min, |, &, xor over
+// Int8 ... UInt64, Float32 and Float64 (Base.cumsum / cumprod / accumulate(op, x; init)).  The
+// kernel and its launch are templates; scan_any*.cu instantiate them an operator family per file.
+//
+// The pipeline of scan.cu (one persistent CTA per SM, 31 work warps + 1 look warp, tiles taken in
+// ticket order, 1-D TMA bulk staging, decoupled lookback of tile k-1 while tile k is summed, second
+// pass from L2), generalised over the element type T and the operator:
+//   * a tile is 124 KiB of input: 15872 elements of 8 bytes ... 126976 of 1 byte; a row is 32 lanes
+//     x one 16-byte vector (2 to 16 elements per lane), a warp owns 8 rows;
+//   * values are accumulated in Traits<T, Op>::A (ki/ops.cuh: 64-bit integers for sums and products
+//     of smaller integers, Float64 for Float32 sums and products) and written as Traits<T, Op>::R
+//     (Int64/UInt64 when widened, Float32 for Float32, T otherwise), as Base.cumsum/cumprod do;
+//   * tile aggregates and prefixes ride in the status words when they fit (4-byte values, 8-byte
+//     integers within 61 bits) and otherwise travel through the lookback's side arrays
+//     (decoupled_lookback_any in ki/lookback.cuh).
+// The Int64 + scan keeps its own kernel (scan.cu), whose values travel packed in the status words.
+//
+// Exclusive scans write op(init, x[1..i-1]) at i (init at the first element); inclusive scans
+// op(init, x[1..i]).  Float sums are deterministic up to the order in which lookback windows find
+// their predecessors, i.e. to Float64 rounding before the final Float32 rounding.
+#pragma once
+
+#include "ki/common.cuh"
+#include "ki/intrinsics.cuh"
+#include "ki/lookback.cuh"
+#include "ki/ops.cuh"
+
+#include <limits>
+
+namespace {
+
+#ifndef KI_SCAN_ANY_SMALL_BATCH
+#define KI_SCAN_ANY_SMALL_BATCH 2
+#endif
+constexpr int kWorkWarps = 31;
+constexpr int kLookWarp = kWorkWarps;
+constexpr int kWorkThreads = 32 * kWorkWarps;
+constexpr int kThreads = kWorkThreads + 32;
+constexpr int kRowsPerWarp = 8;
+constexpr size_t kTileBytes = (size_t)kWorkWarps * kRowsPerWarp * 32 * 16;  // 126976 B
+
+template <class T>
+struct Shape {
+    static constexpr int kE = (int)(16 / sizeof(T));        // elements per lane per row
+    static constexpr int kRow = 32 * kE;                     // elements per row
+    static constexpr int kSpan = kRowsPerWarp * kRow;         // elements per warp
+    static constexpr int kTile = kWorkWarps * kSpan;          // elements per tile
+};
+
+struct AnyArgs {
+    const void* in;
+    void* out;
+    size_t n;
+    uint64_t init_bits;  // init in the accumulation type, as raw bits
+    ki::TileStatus st;
+    unsigned long long* ticket;
+    uint32_t* status;
+    uint64_t timeout_ns;
+    int tma_in;   // input 16-byte aligned: full tiles come in by TMA and as 16-byte rows
+    int vec_out;  // output 16-byte aligned: full tiles leave with 16-byte stores
+};
+
+template <class A>
+struct PendingAny {
+    unsigned long long t;
+    A agg;
+    A tile_excl;
+    A warp_excl[kWorkWarps];
+};
+
+__device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
+
+template <class T, class Op, bool EXCL>
+__global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
+    using Tr = ki::Traits<T, Op>;
+    using A = typename Tr::A;
+    using R = typename Tr::R;
+    using S = Shape<T>;
+    constexpr int kE = S::kE;
+    const ki::OpFn<T, Op> op;
+    const A id = Tr::identity();
+    const A init = ki::from_bits<A>(a.init_bits);
+    const T* in = static_cast<const T*>(a.in);
+    R* out = static_cast<R*>(a.out);
+
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    T* sb = reinterpret_cast<T*>(smem_raw);
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ A warp_tot[kWorkWarps];
+    __shared__ PendingAny<A> slot[2];
+    __shared__ unsigned long long ticket;
+
+    const int tid = threadIdx.x;
+    const int w = tid >> 5;
+    const unsigned lane = tid & 31;
+    const uint64_t ntiles = (a.n + S::kTile - 1) / S::kTile;
+    auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)S::kTile <= a.n; };
+    auto fetch = [&]() {
+        const unsigned long long t = atomicAdd(a.ticket, 1ull);
+        ticket = t;
+        if (bulk_ok(t)) {
+            ki::fence_proxy_async_smem();
+            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kTileBytes);
+            ki::bulk_g2s_keep(sb, in + t * S::kTile, (uint32_t)kTileBytes, &bar);
+        }
+    };
+    if (tid == 0) {
+        ki::mbar_init(&bar, 1);
+        ki::fence_mbar_init();
+        fetch();
+    }
+    __syncthreads();
+
+    uint32_t phase = 0;
+    bool have_old = false;
+    int cur = 0;
+    while (true) {
+        const uint64_t t_new = ticket;
+        const bool new_valid = t_new < ntiles;
+        if (!new_valid && !have_old) break;
+
+        // ---- phase A: fold and publish tile k  ||  look back for tile k-1 ---------------------------
+        if (w == kLookWarp) {
+            if (have_old) {
+                PendingAny<A>& o = slot[cur ^ 1];
+                const A ex = ki::decoupled_lookback_any<1>(a.st, o.t, o.agg, init, id, op, a.status, a.timeout_ns);
+                if (lane == 0) o.tile_excl = ex;
+            }
+        } else if (new_valid) {
+            const size_t first = (size_t)t_new * S::kTile;
+            const int count = (int)min((size_t)S::kTile, a.n - first);
+            if (bulk_ok(t_new)) {
+                if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
+                    ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
+                phase ^= 1u;
+            } else {
+                const T pad = ki::pad_value<T, Op>();
+                for (int i = tid; i < S::kTile; i += kWorkThreads) sb[i] = (i < count) ? in[first + i] : pad;
+                work_sync();
+            }
+            A s = id;
+#pragma unroll
+            for (int j = 0; j < kRowsPerWarp; ++j) {
+                ki::Packed16<T> v;
+                v.raw = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
+#pragma unroll
+                for (int e = 0; e < kE; ++e) s = op(s, Tr::lift(v.get(e)));
+            }
+            s = ki::warpfold(s, op);
+            if (lane == 0) warp_tot[w] = s;
+            work_sync();
+            if (w == 0) {
+                const A x = (lane < (unsigned)kWorkWarps) ? warp_tot[lane] : id;
+                const A inc = ki::warpreduce(x, op);
+                A exc = __shfl_up_sync(0xffffffffu, inc, 1);
+                if (lane == 0) exc = id;
+                const A agg = __shfl_sync(0xffffffffu, inc, kWorkWarps - 1);
+                PendingAny<A>& e = slot[cur];
+                if (lane < (unsigned)kWorkWarps) e.warp_excl[lane] = exc;
+                if (lane == 0) {
+                    e.t = t_new;
+                    e.agg = agg;
+                    ki::publish_aggregate_any(a.st, t_new, agg, init, op);
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- phase B: start tile k+1's load; finish tile k-1 -----------------------------------------
+        if (tid == kLookWarp * 32 && new_valid) fetch();
+        if (w < kWorkWarps && have_old) {
+            const PendingAny<A>& o = slot[cur ^ 1];
+            const size_t first = (size_t)o.t * S::kTile;
+            const int count = (int)min((size_t)S::kTile, a.n - first);
+            const bool full = count == S::kTile;
+            A carry = op(o.tile_excl, o.warp_excl[w]);
+            const T pad = ki::pad_value<T, Op>();
+            // rows in flight: all 8 for 4- and 8-byte elements; 1- and 2-byte elements take more
+            // registers per row on the way out, so they go KI_SCAN_ANY_SMALL_BATCH rows at a time
+            constexpr int kB = sizeof(T) >= 4 ? kRowsPerWarp : KI_SCAN_ANY_SMALL_BATCH;
+#pragma unroll 1
+            for (int j0 = 0; j0 < kRowsPerWarp; j0 += kB) {
+            ki::Packed16<T> v[kB];
+#pragma unroll
+            for (int jj = 0; jj < kB; ++jj) {
+                const int j = j0 + jj;
+                const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
+                if (full && a.tma_in) {
+                    v[jj].raw = __ldcs(reinterpret_cast<const uint4*>(in + first + i));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < kE; ++e) v[jj].set(e, (i + e < count) ? in[first + i + e] : pad);
+                }
+            }
+#pragma unroll
+            for (int jj = 0; jj < kB; ++jj) {
+                const int j = j0 + jj;
+                // the lane's total, the warp's scan of the totals, then the lane's prefixes again on
+                // the way out (no per-element arrays: 16-byte lanes of 1-byte elements stay in registers)
+                A tot = Tr::lift(v[jj].get(0));
+#pragma unroll
+                for (int e = 1; e < kE; ++e) tot = op(tot, Tr::lift(v[jj].get(e)));
+                const A inc = ki::warpreduce(tot, op);
+                A before = __shfl_up_sync(0xffffffffu, inc, 1);
+                if (lane == 0) before = id;
+                A run = op(carry, before);
+                const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
+                if (full && a.vec_out) {
+                    constexpr int kPer = (int)(16 / sizeof(R));  // results per 16-byte store
+                    constexpr int kStores = kE / kPer;
+#pragma unroll
+                    for (int q = 0; q < kStores; ++q) {
+                        alignas(16) R r[kPer];
+#pragma unroll
+                        for (int p = 0; p < kPer; ++p) {
+                            const A x = Tr::lift(v[jj].get(q * kPer + p));
+                            if (EXCL) {
+                                r[p] = Tr::lower(run);
+                                run = op(run, x);
+                            } else {
+                                run = op(run, x);
+                                r[p] = Tr::lower(run);
+                            }
+                        }
+                        __stcs(reinterpret_cast<uint4*>(out + first + i) + q, *reinterpret_cast<const uint4*>(r));
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < kE; ++e) {
+                        const A x = Tr::lift(v[jj].get(e));
+                        R r;
+                        if (EXCL) {
+                            r = Tr::lower(run);
+                            run = op(run, x);
+                        } else {
+                            run = op(run, x);
+                            r = Tr::lower(run);
+                        }
+                        if (i + e < count) out[first + i + e] = r;
+                    }
+                }
+                carry = op(carry, __shfl_sync(0xffffffffu, inc, 31));
+            }
+            }
+        }
+        __syncthreads();
+        have_old = new_valid;
+        cur ^= 1;
+    }
+}
+
+template <class T, class Op>
+int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, size_t n, const void* h_init, cudaStream_t s) {
+    using Tr = ki::Traits<T, Op>;
+    using A = typename Tr::A;
+    using R = typename Tr::R;
+    using S = Shape<T>;
+    if (!ki::aligned(d_in, sizeof(T)) || !ki::aligned(d_out, sizeof(R)))
+        return ki::set_error(ctx, KI_ERR_ARG, "scan: misaligned input or output");
+    const uintptr_t i0 = (uintptr_t)d_in, o0 = (uintptr_t)d_out;
+    const uintptr_t ib = n * sizeof(T), ob = n * sizeof(R);
+    if (!(i0 == o0 && sizeof(T) == sizeof(R)) && i0 < o0 + ob && o0 < i0 + ib)
+        return ki::set_error(ctx, KI_ERR_ARG, "scan: input and output overlap (only an exact in-place scan is allowed)");
+    // init: a host value of the result type, converted to the accumulation type; else the identity
+    A init;
+    if (h_init) {
+        R r;
+        memcpy(&r, h_init, sizeof(R));
+        if constexpr (std::is_same<Op, ki::JAdd>::value || std::is_same<Op, ki::JMul>::value) init = (A)r;
+        else init = Tr::lift(r);
+    } else if constexpr (std::is_same<Op, ki::JAdd>::value) {
+        init = A(0);
+    } else if constexpr (std::is_same<Op, ki::JMul>::value) {
+        init = A(1);
+    } else if constexpr (ki::IsBitwise<Op>::value) {
+        init = Tr::identity();
+    } else {
+        using TT = typename std::conditional<std::is_floating_point<T>::value, T, double>::type;
+        if constexpr (std::is_floating_point<T>::value)
+            init = Tr::lift(std::is_same<Op, ki::JMax>::value ? -std::numeric_limits<TT>::infinity()
+                                                               : std::numeric_limits<TT>::infinity());
+        else
+            init = std::is_same<Op, ki::JMax>::value ? std::numeric_limits<A>::lowest() : std::numeric_limits<A>::max();
+    }
+    const size_t ntiles = (n + S::kTile - 1) / S::kTile;
+    const size_t words_off = 256;
+    void* base = nullptr;
+    int rc = ki::ensure_region(ctx, KI_REG_SCAN_ANY, words_off + ntiles * 24, &base);
+    if (rc) return rc;
+    char* b = static_cast<char*>(base);
+    KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * sizeof(uint64_t), s));
+    AnyArgs a;
+    a.in = d_in;
+    a.out = d_out;
+    a.n = n;
+    a.init_bits = 0;
+    memcpy(&a.init_bits, &init, sizeof(A));
+    a.st.words = reinterpret_cast<uint64_t*>(b + words_off);
+    a.st.aggs = reinterpret_cast<int64_t*>(b + words_off + ntiles * 8);
+    a.st.incls = reinterpret_cast<int64_t*>(b + words_off + ntiles * 16);
+    a.ticket = reinterpret_cast<unsigned long long*>(b);
+    a.status = ctx->d_status;
+    a.timeout_ns = ctx->wait_timeout_ns;
+    a.tma_in = ki::aligned(d_in, 16);
+    a.vec_out = ki::aligned(d_out, 16);
+    size_t grid = (size_t)ctx->sm_count;
+    if (grid > ntiles) grid = ntiles;
+    if (excl) {
+        KI_CUDA(ctx, cudaFuncSetAttribute(scan_any_kernel<T, Op, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)kTileBytes));
+        scan_any_kernel<T, Op, true><<<(unsigned)grid, kThreads, kTileBytes, s>>>(a);
+    } else {
+        KI_CUDA(ctx, cudaFuncSetAttribute(scan_any_kernel<T, Op, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)kTileBytes));
+        scan_any_kernel<T, Op, false><<<(unsigned)grid, kThreads, kTileBytes, s>>>(a);
+    }
+    return ki::check_launch(ctx, "scan_any_kernel launch");
+}
+
+template <class Op>
+int scan_op(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, size_t n, const void* h_init,
+            cudaStream_t s) {
+    constexpr int kBad = -1000;
+    const int rc = ki::with_dtype(dtype, kBad, [&](auto tag) -> int {
+        using T = decltype(tag);
+        if constexpr (ki::op_takes<T, Op>()) return scan_launch<T, Op>(ctx, excl, d_in, d_out, n, h_init, s);
+        else return kBad;
+    });
+    if (rc == kBad) return ki::set_error(ctx, KI_ERR_ARG, "scan: the operator does not take this element type");
+    return rc;
+}
+
+}  // namespace
+
+// One per operator, defined in scan_any*.cu.
+#define KI_SCAN_ANY_ENTRY(name) \
+    __attribute__((visibility("hidden"))) int name(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, size_t n, const void* h_init, cudaStream_t s)
+KI_SCAN_ANY_ENTRY(ki_scan_any_add);
+KI_SCAN_ANY_ENTRY(ki_scan_any_mul);
+KI_SCAN_ANY_ENTRY(ki_scan_any_max);
+KI_SCAN_ANY_ENTRY(ki_scan_any_min);
+KI_SCAN_ANY_ENTRY(ki_scan_any_or);
+KI_SCAN_ANY_ENTRY(ki_scan_any_and);
+KI_SCAN_ANY_ENTRY(ki_scan_any_xor);

@@ -425,6 +425,76 @@ def vcopy(dst, src, nbytes: Optional[int] = None, dst_offset: int = 0, src_offse
     return dst
 
 
+def vcopy_2d(dst, dpitch: int, src, spitch: int, width: int, height: int, dst_offset: int = 0, src_offset: int = 0,
+             stream=None):
+    """copyto! of ``height`` rows of ``width`` bytes: row r from byte src_offset + r*spitch of ``src`` to
+    byte dst_offset + r*dpitch of ``dst`` (any alignment, any pitch >= width)."""
+    d = _dev(dst)
+    if width > 0 and height > 0:
+        last_d = dst_offset + (height - 1) * dpitch + width
+        last_s = src_offset + (height - 1) * spitch + width
+        if min(dst_offset, src_offset) < 0 or last_d > dst.numel() * dst.element_size() or \
+                last_s > src.numel() * src.element_size():
+            raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_2d: range outside the tensors")
+    context(d).call("ki_vcopy_2d", ctypes.c_void_p(dst.data_ptr() + dst_offset), int(dpitch),
+                    ctypes.c_void_p(src.data_ptr() + src_offset), int(spitch), int(width), int(height),
+                    _stream_ptr(stream, d))
+    return dst
+
+
+def vcopy_strided(dst, dst_stride: int, src, src_stride: int, count: int, dst_start: int = 0, src_start: int = 0,
+                  stream=None):
+    """dst[dst_start + i*dst_stride] = src[src_start + i*src_stride] for i < count, in elements of the
+    tensors' (equal) element size; strides of either sign, as Julia's strided and reversed views."""
+    d = _dev(dst)
+    es = dst.element_size()
+    if src.element_size() != es:
+        raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_strided: element sizes differ")
+    if count > 0:
+        for t, st, n0 in ((dst, dst_stride, dst_start), (src, src_stride, src_start)):
+            last = n0 + (count - 1) * st
+            if min(n0, last) < 0 or max(n0, last) >= t.numel():
+                raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_strided: range outside the tensors")
+    context(d).call("ki_vcopy_strided", ctypes.c_void_p(dst.data_ptr() + dst_start * es), int(dst_stride),
+                    ctypes.c_void_p(src.data_ptr() + src_start * es), int(src_stride), es, int(count),
+                    _stream_ptr(stream, d))
+    return dst
+
+
+def copyto(dst, src, stream=None):
+    """copyto!(dst, src) for device views of the same shape and element size: contiguous ranges go
+    through vcopy, 1-D strided views through vcopy_strided, 2-D views with contiguous rows through
+    vcopy_2d (one row per leading index)."""
+    if tuple(dst.shape) != tuple(src.shape) or dst.element_size() != src.element_size():
+        raise KIArgumentError(_abi.KI_ERR_ARG, "copyto: shapes or element sizes differ")
+    es = dst.element_size()
+    if dst.numel() == 0:
+        return dst
+    if dst.is_contiguous() and src.is_contiguous():
+        return _copy_raw("ki_vcopy", dst, src, dst.numel() * es, stream)
+    if dst.dim() == 1:
+        return _copy_raw("ki_vcopy_strided", dst, src, dst.numel(), stream, dst.stride(0), src.stride(0), es)
+    if dst.dim() == 2 and dst.stride(1) == 1 and src.stride(1) == 1:
+        return _copy_raw("ki_vcopy_2d", dst, src, dst.shape[1] * es, stream, dst.stride(0) * es, src.stride(0) * es,
+                         dst.shape[0])
+    raise KIArgumentError(_abi.KI_ERR_ARG, "copyto: 1-D views, or 2-D views with contiguous rows")
+
+
+def _copy_raw(fn, dst, src, n, stream, *extra):
+    d = _dev(dst)
+    pd, ps = ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src.data_ptr())
+    s = _stream_ptr(stream, d)
+    if fn == "ki_vcopy":
+        context(d).call(fn, pd, ps, int(n), s)
+    elif fn == "ki_vcopy_strided":
+        dstride, sstride, es = extra
+        context(d).call(fn, pd, int(dstride), ps, int(sstride), int(es), int(n), s)
+    else:
+        dpitch, spitch, height = extra
+        context(d).call(fn, pd, int(dpitch), ps, int(spitch), int(n), int(height), s)
+    return dst
+
+
 def vcopy_host(dst, src, nbytes: Optional[int] = None, dst_offset: int = 0, src_offset: int = 0, device: int = 0,
                stream=None):
     """copyto! between two host (CPU) tensors through device ``device``: chunks go to the device, are
@@ -475,21 +545,35 @@ def warpreduce_scan(x, out=None, seed: int = 0, stream=None):
     return out
 
 
-# Result dtype of Base.sum / cumsum (add_sum widens small integers) and of maximum/minimum (same type).
 def _result_dtype(dtype, op: str):
+    """Base's result type: sums and products (add_sum / mul_prod) widen integers narrower than 64
+    bits to Int64 / UInt64; every other operator keeps the element type."""
     torch = _torch()
-    if op in ("+", "add") and dtype in (torch.int32, torch.uint32):
-        return torch.int64 if dtype == torch.int32 else torch.uint64
+    if op in ("+", "add", "*", "mul"):
+        if dtype in (torch.int8, torch.int16, torch.int32):
+            return torch.int64
+        if dtype in (torch.uint8, torch.uint16, torch.uint32):
+            return torch.uint64
     return dtype
 
 
-_GENERIC_OPS = {"+": 0, "add": 0, "max": 1, "min": 2}
+_GENERIC_OPS = {"+": 0, "add": 0, "max": 1, "min": 2, "|": 3, "or": 3, "&": 4, "and": 4, "xor": 5, "*": 6, "mul": 6}
+
+
+def _np_dtype(t):
+    import numpy as np
+
+    name = str(t).replace("torch.", "")
+    if name not in _abi.DTYPE:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"unsupported dtype {t}")
+    return np.dtype(name)
 
 
 def reduce(x, op: str = "+", out=None, stream=None):
-    """sum / maximum / minimum of Int32, UInt32, Int64, UInt64, Float32 or Float64 ``x`` with Julia Base
-    semantics (the device-wide @warpfold): Int32/UInt32 sums widen to 64 bits, Float32 sums
-    accumulate in Float64, maximum/minimum propagate NaN.  Returns a device scalar."""
+    """sum / prod / maximum / minimum / reduce(|, &, xor) of Int8 ... UInt64, Float32 or Float64 ``x``
+    with Julia Base semantics (the device-wide @warpfold): sums and products of narrower integers
+    widen to 64 bits, Float32 sums and products accumulate in Float64, maximum/minimum propagate
+    NaN; the bitwise operators take integers.  Returns a device scalar."""
     torch = _torch()
     d = _dev(x)
     if op not in _GENERIC_OPS:
@@ -502,8 +586,8 @@ def reduce(x, op: str = "+", out=None, stream=None):
 
 
 def reduce_rows(x, op: str = "+", out=None, stream=None):
-    """One sum / maximum / minimum per row of a 2-D ``x`` whose rows are contiguous (``x.stride(1) == 1``;
-    ``x.stride(0)`` is the leading dimension).  Result types as ``reduce``."""
+    """One reduction per row (the operators of ``reduce``) of a 2-D ``x`` whose rows are contiguous
+    (``x.stride(1) == 1``; ``x.stride(0)`` is the leading dimension).  Result types as ``reduce``."""
     torch = _torch()
     d = _dev(x)
     if op not in _GENERIC_OPS:
@@ -519,9 +603,9 @@ def reduce_rows(x, op: str = "+", out=None, stream=None):
 
 
 def scan(x, op: str = "+", exclusive: bool = False, init=None, out=None, stream=None):
-    """accumulate(op, x; init) / cumsum for Int32, UInt32, Int64, UInt64, Float32 or Float64 ``x``
-    (the device-wide @warpreduce).  The result has Base's type (widened for Int32/UInt32 sums);
-    ``exclusive`` shifts it by one element and starts at ``init`` (the identity when None)."""
+    """accumulate(op, x; init) / cumsum / cumprod for the operators and types of ``reduce`` (the
+    device-wide @warpreduce).  The result has Base's type (widened for sums and products of narrower
+    integers); ``exclusive`` shifts it by one element and starts at ``init`` (the identity when None)."""
     import numpy as np
 
     torch = _torch()
@@ -532,9 +616,7 @@ def scan(x, op: str = "+", exclusive: bool = False, init=None, out=None, stream=
     out = torch.empty(x.shape, dtype=rd, device=x.device) if out is None else out
     init_buf = None
     if init is not None:
-        np_dt = {torch.int32: np.int32, torch.uint32: np.uint32, torch.int64: np.int64, torch.uint64: np.uint64,
-                 torch.float32: np.float32, torch.float64: np.float64}[rd]
-        init_buf = np.array([init], dtype=np_dt)
+        init_buf = np.array([init], dtype=_np_dtype(rd))
     context(d).call("ki_scan", _GENERIC_OPS[op], _dtype_code(x), int(bool(exclusive)), _ptr(x), _ptr(out), x.numel(),
                     ctypes.c_void_p(init_buf.ctypes.data) if init_buf is not None else None, _stream_ptr(stream, d))
     return out

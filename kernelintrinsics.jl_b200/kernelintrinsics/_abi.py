@@ -41,6 +41,8 @@ SIGNATURES = {
     "ki_ctx_set_wait_timeout_ns": (_i32, [_vp, _u64]),
     "ki_vcopy": (_i32, [_vp, _vp, _vp, _sz, _vp]),
     "ki_vcopy_host": (_i32, [_vp, _vp, _vp, _sz, _vp]),
+    "ki_vcopy_2d": (_i32, [_vp, _vp, _sz, _vp, _sz, _sz, _sz, _vp]),
+    "ki_vcopy_strided": (_i32, [_vp, _vp, _i64, _vp, _i64, _sz, _sz, _vp]),
     "ki_reduce_sum_f32": (_i32, [_vp, _vp, _sz, _vp, _vp, _vp]),
     "ki_reduce_sum_i64": (_i32, [_vp, _vp, _sz, _vp, _vp]),
     "ki_scan_inclusive_i64": (_i32, [_vp, _vp, _vp, _sz, _i64, _vp]),

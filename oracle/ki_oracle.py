@@ -182,22 +182,40 @@ def cumsum_i64(x: np.ndarray, seed: int = 0, nthreads: int = 0) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------------------------
-# Device-wide reduce / scan for +, max, min (the device-wide uses of @warpfold and @warpreduce,
-# src/warp.jl:273-282 and :226-237, which take any operator): Julia Base semantics of
-# sum / maximum / minimum and cumsum / accumulate(op, x; init).
-#   * +    Int32 -> Int64 and UInt32 -> UInt64 (Base.add_sum widens), Int64/UInt64 wrap,
-#          floats in Float64 (the device's Float32 result is compared within a tolerance);
-#   * max  NaN wins, +0.0 > -0.0 (Base.max); min: NaN wins, -0.0 < +0.0 (Base.min).
+# Device-wide reduce / scan for +, *, max, min, |, &, xor (the device-wide uses of @warpfold and
+# @warpreduce, src/warp.jl:273-282 and :226-237, which take any operator): Julia Base semantics of
+# sum / prod / maximum / minimum / reduce(op, x) and cumsum / cumprod / accumulate(op, x; init).
+#   * + and *  integers narrower than 64 bits widen to Int64 / UInt64 (Base.add_sum, Base.mul_prod),
+#          64-bit integers wrap, floats in Float64 (the device's Float32 result is compared within a
+#          tolerance);
+#   * max  NaN wins, +0.0 > -0.0 (Base.max); min: NaN wins, -0.0 < +0.0 (Base.min);
+#   * |, &, xor  integers, in their own type.
 # ---------------------------------------------------------------------------------------------
+_BITWISE = {"|": np.bitwise_or, "&": np.bitwise_and, "xor": np.bitwise_xor}
+
+
 def result_dtype(dtype, op: str):
     dtype = np.dtype(dtype)
-    if op == "+" and dtype == np.int32:
-        return np.dtype(np.int64)
-    if op == "+" and dtype == np.uint32:
-        return np.dtype(np.uint64)
-    if op == "+" and dtype.kind == "f":
-        return np.dtype(np.float64)
+    if op in ("+", "*"):
+        if dtype.kind == "f":
+            return np.dtype(np.float64)
+        if dtype.itemsize < 8:
+            return np.dtype(np.int64 if dtype.kind == "i" else np.uint64)
     return dtype
+
+
+def identity(op: str, dtype):
+    """The operator's identity in the result type (what an exclusive scan starts from)."""
+    rd = result_dtype(dtype, op)
+    if op in ("+", "|", "xor"):
+        return rd.type(0)
+    if op == "*":
+        return rd.type(1)
+    if op == "&":
+        return rd.type(-1) if rd.kind == "i" else np.iinfo(rd).max
+    if rd.kind == "f":
+        return rd.type(-np.inf if op == "max" else np.inf)
+    return np.iinfo(rd).min if op == "max" else np.iinfo(rd).max
 
 
 def _float_keys(x: np.ndarray, op: str) -> np.ndarray:
@@ -224,10 +242,20 @@ def accumulate(op: str, x: np.ndarray, init=None, exclusive: bool = False) -> np
     """accumulate(op, x; init) with Base semantics; exclusive shifts by one and starts at init."""
     x = np.ascontiguousarray(x)
     rd = result_dtype(x.dtype, op)
-    if op == "+":
-        v = np.cumsum(x.astype(rd), dtype=rd)  # numpy wraps integer overflow like Base
+    if op in ("+", "*"):
+        acc = np.cumsum if op == "+" else np.cumprod
+        with np.errstate(over="ignore"):
+            v = acc(x.astype(rd), dtype=rd)  # numpy wraps integer overflow like Base
+            if init is not None:
+                t = rd.type(init)
+                v = (v + t if op == "+" else v * t).astype(rd)
+    elif op in _BITWISE:
+        if x.dtype.kind not in "iu":
+            raise ValueError(f"{op} takes integers")
+        seq = x if init is None else np.concatenate([np.array([init], dtype=x.dtype), x])
+        v = _BITWISE[op].accumulate(seq)
         if init is not None:
-            v = (v + rd.type(init)).astype(rd) if rd.kind != "f" else v + float(init)
+            v = v[1:]
     elif x.dtype.kind == "f":
         keys = _float_keys(x, op)
         if init is not None:
@@ -244,21 +272,17 @@ def accumulate(op: str, x: np.ndarray, init=None, exclusive: bool = False) -> np
     if not exclusive:
         return v
     if init is None:
-        if op == "+":
-            init = 0
-        elif rd.kind == "f":
-            init = -np.inf if op == "max" else np.inf
-        else:
-            init = np.iinfo(rd).min if op == "max" else np.iinfo(rd).max
+        init = identity(op, x.dtype)
     return np.concatenate([np.array([init], dtype=rd), v[:-1]])
 
 
 def reduce_op(op: str, x: np.ndarray):
-    """sum / maximum / minimum with Base semantics (raises on an empty maximum / minimum)."""
+    """sum / prod / maximum / minimum / reduce(op, x) with Base semantics (an empty sum is 0, an empty
+    product 1; the other operators raise on an empty collection)."""
     x = np.ascontiguousarray(x)
     if x.size == 0:
-        if op == "+":
-            return result_dtype(x.dtype, op).type(0)
+        if op in ("+", "*"):
+            return identity(op, x.dtype)
         raise ValueError("reducing over an empty collection is not allowed")
     return accumulate(op, x)[-1]
 
@@ -276,6 +300,24 @@ def filter_gt_f32(x: np.ndarray, thr: float, index_base: int = 1, nthreads: int 
 def copy_bytes(dst: np.ndarray, src: np.ndarray, nthreads: int = 0) -> None:
     assert dst.nbytes >= src.nbytes
     lib().ko_copy_bytes(_ptr(dst), _ptr(src), src.nbytes, nthreads)
+
+
+def copy_2d(dst: np.ndarray, dpitch: int, src: np.ndarray, spitch: int, width: int, height: int,
+            dst_offset: int = 0, src_offset: int = 0) -> None:
+    """copyto! of a strided byte matrix, one row at a time: the element-by-element semantics of the
+    reference's AbstractArray fallback (_vload_batch / _vstore_batch!, src/vectorization.jl:426-448)
+    applied to bytes.  dst and src are 1-D uint8 arrays."""
+    for r in range(height):
+        d0, s0 = dst_offset + r * dpitch, src_offset + r * spitch
+        dst[d0:d0 + width] = src[s0:s0 + width]
+
+
+def copy_strided(dst: np.ndarray, dst_stride: int, src: np.ndarray, src_stride: int, count: int,
+                 dst_start: int = 0, src_start: int = 0) -> None:
+    """dst[dst_start + i*dst_stride] = src[src_start + i*src_stride] for i < count (element strides of
+    either sign), in index order."""
+    i = np.arange(count, dtype=np.int64)
+    dst[dst_start + i * dst_stride] = src[src_start + i * src_stride]
 
 
 def gemm_e4m3_rows(A: np.ndarray, B: np.ndarray, r0: int, r1: int, scale: float = 1.0,

@@ -1,8 +1,9 @@
-"""GPU: device-wide reduce and scan for +, max, min over Int32/UInt32/Int64/UInt64/Float32/Float64
-(ki_reduce, ki_scan) against the oracle's Julia Base semantics.
+"""GPU: device-wide reduce and scan for +, *, max, min, |, &, xor over Int8 ... UInt64, Float32 and
+Float64 (ki_reduce, ki_scan, ki_reduce_rows) against the oracle's Julia Base semantics.
 
 Integers are bit-exact.  Float sums: |device - Float64 oracle| <= 1e-5*log2(n) * (running sum of |x|),
-the tolerance the workload definition states for Float32 reduce/scan.  max/min are exact, NaN included.
+the tolerance the workload definition states for Float32 reduce/scan; float products: within
+1e-5*log2(n) of the Float64 product, relative.  max/min are exact, NaN included.
 """
 from __future__ import annotations
 
@@ -13,13 +14,22 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-NP_TYPES = [np.int32, np.uint32, np.int64, np.uint64, np.float32, np.float64]
-OPS = ["+", "max", "min"]
+NP_TYPES = [np.int8, np.uint8, np.int16, np.uint16, np.int32, np.uint32, np.int64, np.uint64, np.float32, np.float64]
+OPS = ["+", "*", "max", "min", "|", "&", "xor"]
+BITWISE = ("|", "&", "xor")
+
+
+def _cases():
+    """(dtype, op) pairs the operators take: the bitwise ones take integers only."""
+    return [pytest.param(dt, op, id=f"{op}-{np.dtype(dt).name}") for op in OPS for dt in NP_TYPES
+            if not (op in BITWISE and np.dtype(dt).kind == "f")]
 
 
 def _data(dt, n, seed, op="max"):
     rng = np.random.default_rng(seed)
     dt = np.dtype(dt)
+    if dt.kind == "f" and op == "*":  # log-normal factors: the product's log is a zero-mean walk
+        return np.exp(0.01 * rng.standard_normal(n)).astype(dt)
     if dt.kind == "f":
         x = rng.standard_normal(n).astype(dt)
         if n > 10 and op != "+":  # for max/min: signed zeros, infinities (NaN has its own test)
@@ -27,9 +37,11 @@ def _data(dt, n, seed, op="max"):
             x[rng.integers(0, n, 3)] = 0.0
             x[rng.integers(0, n, 1)] = np.inf if seed % 2 else -np.inf
         return x
-    if dt.kind == "u":
-        return rng.integers(0, np.iinfo(dt).max, n, dtype=dt, endpoint=True)
-    return rng.integers(np.iinfo(dt).min, np.iinfo(dt).max, n, dtype=dt, endpoint=True)
+    info = np.iinfo(dt)
+    x = rng.integers(info.min, info.max, n, dtype=dt, endpoint=True)
+    if op == "*":  # odd factors: the wrapped product never collapses to zero
+        x |= dt.type(1)
+    return x
 
 
 def _to_dev(x, dev):
@@ -39,7 +51,11 @@ def _to_dev(x, dev):
 
 
 def _check(got, want, x, op):
-    if np.dtype(want.dtype).kind == "f" and op == "+":
+    if np.dtype(want.dtype).kind == "f" and op == "*":
+        n = max(2, x.size)
+        err = np.abs(got.astype(np.float64) - want)
+        assert (err <= 1e-5 * math.log2(n) * np.abs(want) + 1e-300).all(), float((err / np.abs(want)).max())
+    elif np.dtype(want.dtype).kind == "f" and op == "+":
         n = max(2, x.size)
         scale = np.cumsum(np.abs(x.astype(np.float64)))
         err = np.abs(got.astype(np.float64) - want)
@@ -52,11 +68,10 @@ def _check(got, want, x, op):
         assert np.array_equal(got, want)
 
 
-SIZES = [1, 2, 31, 33, 1000, 15871, 15872, 15873, 31743, 31744, 31745, 100_003, (1 << 20) + 3]
+SIZES = [1, 2, 31, 33, 1000, 15871, 15872, 15873, 31743, 31744, 31745, 63489, 100_003, 126977, 253952, (1 << 20) + 3]
 
 
-@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
-@pytest.mark.parametrize("op", OPS)
+@pytest.mark.parametrize("dt,op", _cases())
 def test_scan_inclusive_and_exclusive(KI, oracle, dev, dt, op):
     for k, n in enumerate(SIZES):
         x = _data(dt, n, 10 * k + 1, op)
@@ -73,11 +88,12 @@ def test_scan_init_misaligned_and_in_place(KI, oracle, dev, dt):
     import torch
 
     n = 3 * 31744 + 11
-    x = _data(dt, n + 1, 7, "+")
-    base = _to_dev(x, dev)
-    xs = base[1:]  # 4- or 8-byte offset: the plain-load path
     init = 5 if np.dtype(dt).kind != "f" else 0.25
     for op in OPS:
+        if op in BITWISE and np.dtype(dt).kind == "f":
+            continue
+        x = _data(dt, n + 1, 7, op)
+        xs = _to_dev(x, dev)[1:]  # 4- or 8-byte offset: the plain-load path
         got = KI.scan(xs, op, init=init).cpu().numpy()
         want = oracle.accumulate(op, x[1:], init=init)
         _check(got, want, x[1:], op)
@@ -107,8 +123,7 @@ def test_scan_nan_and_extremes(KI, oracle, dev):
     assert got.dtype == np.int64 and np.array_equal(got, oracle.accumulate("+", i32))
 
 
-@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
-@pytest.mark.parametrize("op", OPS)
+@pytest.mark.parametrize("dt,op", _cases())
 def test_reduce(KI, oracle, dev, dt, op):
     for k, n in enumerate([1, 7, 33, 4099, 1 << 16, (1 << 22) + 5]):
         x = _data(dt, n, 100 + k, op)
@@ -116,6 +131,8 @@ def test_reduce(KI, oracle, dev, dt, op):
         want = np.array([oracle.reduce_op(op, x)])
         if np.dtype(dt).kind == "f" and op == "+":
             assert abs(float(got[0]) - float(want[0])) <= 1e-5 * math.log2(max(2, n)) * float(np.abs(x.astype(np.float64)).sum())
+        elif np.dtype(dt).kind == "f" and op == "*":
+            assert abs(float(got[0]) - float(want[0])) <= 1e-5 * math.log2(max(2, n)) * abs(float(want[0])) + 1e-300
         else:
             _check(got, want.astype(got.dtype), x, op)
     KI.context(0).check()
@@ -126,8 +143,15 @@ def test_reduce_empty_and_nan(KI, dev):
 
     e = torch.empty(0, dtype=torch.float32, device=dev)
     assert KI.reduce(e, "+").item() == 0.0
+    assert KI.reduce(e, "*").item() == 1.0
+    assert KI.reduce(torch.empty(0, dtype=torch.uint8, device=dev), "*").item() == 1
     with pytest.raises(KI.KIArgumentError):
         KI.reduce(e, "max")
+    for op in ("|", "&", "xor"):
+        with pytest.raises(KI.KIArgumentError):
+            KI.reduce(torch.empty(0, dtype=torch.int16, device=dev), op)
+        with pytest.raises(KI.KIArgumentError):  # the bitwise operators take integers
+            KI.reduce(torch.ones(8, dtype=torch.float64, device=dev), op)
     x = torch.tensor([1.0, float("nan"), 3.0] * 5000, dtype=torch.float64, device=dev)
     assert math.isnan(KI.reduce(x, "max").item()) and math.isnan(KI.reduce(x, "min").item())
     z = torch.tensor([-0.0, 0.0, -0.0], dtype=torch.float32, device=dev)
@@ -154,8 +178,7 @@ def test_scan_config_size_f32(KI, dev):
 ROW_SHAPES = [(1, 1), (3, 5), (1000, 33), (257, 2048), (7, 2049), (5, 100_003), (2, (1 << 21) + 5), (600, 4096)]
 
 
-@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
-@pytest.mark.parametrize("op", OPS)
+@pytest.mark.parametrize("dt,op", _cases())
 def test_reduce_rows(KI, oracle, dev, dt, op):
     """Segmented reduce (one result per row), with padded rows (ld > cols) and unaligned starts."""
     for k, (rows, cols) in enumerate(ROW_SHAPES):
@@ -172,6 +195,9 @@ def test_reduce_rows(KI, oracle, dev, dt, op):
                 if np.dtype(dt).kind == "f" and op == "+":
                     bound = 1e-5 * math.log2(max(2, cols)) * float(np.abs(m[r, :cols].astype(np.float64)).sum())
                     assert abs(float(g[0]) - float(want[0])) <= bound, (rows, cols, r)
+                elif np.dtype(dt).kind == "f" and op == "*":
+                    bound = 1e-5 * math.log2(max(2, cols)) * abs(float(want[0])) + 1e-300
+                    assert abs(float(g[0]) - float(want[0])) <= bound, (rows, cols, r)
                 else:
                     _check(g, want.astype(g.dtype), m[r, :cols], op)
     KI.context(0).check()
@@ -182,5 +208,8 @@ def test_reduce_rows_empty_rows(KI, dev):
 
     x = torch.empty((4, 0), dtype=torch.float32, device=dev)
     assert KI.reduce_rows(x, "+").tolist() == [0.0] * 4
-    with pytest.raises(KI.KIArgumentError):
-        KI.reduce_rows(x, "max")
+    assert KI.reduce_rows(x, "*").tolist() == [1.0] * 4
+    assert KI.reduce_rows(torch.empty((3, 0), dtype=torch.int8, device=dev), "*").tolist() == [1] * 3
+    for op in ("max", "|"):
+        with pytest.raises(KI.KIArgumentError):
+            KI.reduce_rows(torch.empty((4, 0), dtype=torch.int32, device=dev), op)

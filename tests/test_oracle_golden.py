@@ -180,3 +180,44 @@ def test_accumulate_matches_scalar_base_semantics(oracle):
     assert oracle.accumulate("+", i64).tolist() == [2**63 - 1, -2**63]
     assert oracle.accumulate("+", np.array([1, 2, 3], dtype=np.int64), init=10, exclusive=True).tolist() == [10, 11, 13]
     assert oracle.reduce_op("+", np.zeros(0, dtype=np.int32)) == 0
+
+
+def test_accumulate_products_bitwise_and_small_integers(oracle):
+    """cumprod / accumulate(|, &, xor) and the widening of Int8/Int16/UInt8/UInt16 (Base.add_sum and
+    Base.mul_prod widen them to 64 bits; the bitwise operators keep the type), against scalar loops
+    in Python integers reduced modulo 2^64."""
+    rng = np.random.default_rng(11)
+
+    def wrap(v, signed):
+        v &= (1 << 64) - 1
+        return v - (1 << 64) if signed and v >= 1 << 63 else v
+
+    for dt in (np.int8, np.uint8, np.int16, np.uint16, np.int32, np.uint32, np.int64, np.uint64):
+        info = np.iinfo(dt)
+        x = rng.integers(info.min, info.max, 300, dtype=dt, endpoint=True)
+        signed = info.min < 0
+        for op in ("+", "*"):
+            got = oracle.accumulate(op, x)
+            assert got.dtype == (np.int64 if signed else np.uint64)
+            acc = 0 if op == "+" else 1
+            for i, v in enumerate(x.tolist()):
+                acc = wrap(acc + v if op == "+" else acc * v, signed)
+                assert int(got[i]) == acc, (dt, op, i)
+        for op, f in (("|", lambda a, b: a | b), ("&", lambda a, b: a & b), ("xor", lambda a, b: a ^ b)):
+            got = oracle.accumulate(op, x)
+            assert got.dtype == np.dtype(dt)
+            acc = int(x[0])
+            for i, v in enumerate(x.tolist()):
+                acc = v if i == 0 else f(acc, v)
+                assert int(got[i]) == acc, (dt, op, i)
+            ex = oracle.accumulate(op, x, exclusive=True)
+            assert int(ex[0]) == int(oracle.identity(op, dt)) and np.array_equal(ex[1:], got[:-1])
+    assert oracle.reduce_op("*", np.zeros(0, dtype=np.int8)) == 1
+    assert oracle.identity("&", np.uint16) == 0xFFFF and oracle.identity("&", np.int16) == -1
+    f = np.array([1.5, -2.0, 0.25], dtype=np.float32)
+    assert oracle.accumulate("*", f).tolist() == [1.5, -3.0, -0.75]
+    assert oracle.accumulate("*", f, init=2.0, exclusive=True).tolist() == [2.0, 3.0, -6.0]
+    with pytest.raises(ValueError):
+        oracle.reduce_op("|", np.zeros(0, dtype=np.int32))
+    with pytest.raises(ValueError):
+        oracle.accumulate("xor", f)

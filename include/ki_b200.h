@@ -163,6 +163,14 @@ int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size
  * ki_scan_inclusive_i64. */
 int ki_scan(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in, void* d_out, size_t n,
             const void* h_init, void* stream);
+/* Segmented scan: one ki_scan per row of a rows x cols row-major matrix, every row starting from
+ * h_init (Base.accumulate(op, A; dims) along the contiguous dimension: cumsum(A; dims=1) of a
+ * column-major Julia matrix has rows = its columns).  Row r is read at d_in + r*ld_in and written at
+ * d_out + r*ld_out (elements of the input and of the result type; ld >= cols when rows > 1).
+ * Operators, types, result types and exclusive as ki_scan; in place when the input and result
+ * types have the same size and ld_in == ld_out. */
+int ki_scan_rows(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in, size_t ld_in, void* d_out,
+                 size_t ld_out, size_t rows, size_t cols, const void* h_init, void* stream);
 
 /* Allocation-free scan.  No counterpart in the reference.
  * For callers that cannot allocate device memory: code running while a CUDA graph is captured,

@@ -200,19 +200,26 @@ __device__ __forceinline__ void publish_any(TileStatus st, uint64_t t, uint64_t 
     }
 }
 
+// head: tile t starts a segment (tile 0, or the first tile of a row in a segmented scan); its
+// inclusive prefix is op(init, agg) at once, and no lookback passes it.
+template <class A, class F>
+__device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op, bool head) {
+    if (head) publish_any(st, t, kFlagPrefix, op(init, agg));
+    else publish_any(st, t, kFlagAgg, agg);
+}
 template <class A, class F>
 __device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op) {
-    if (t == 0) publish_any(st, 0, kFlagPrefix, op(init, agg));
-    else publish_any(st, t, kFlagAgg, agg);
+    publish_aggregate_any(st, t, agg, init, op, t == 0);
 }
 
 // Run by all 32 lanes of one warp after publish_aggregate_any(t).  Returns the exclusive prefix of
-// tile t (init for tile 0) and publishes tile t's inclusive prefix.
+// tile t (init for a head tile) and publishes tile t's inclusive prefix.  The walk stops at the
+// nearest inclusive prefix, so it never crosses a head tile into an earlier segment.
 template <int K, class A, class F>
 __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
-                                                    uint32_t* status, uint64_t timeout_ns) {
+                                                    uint32_t* status, uint64_t timeout_ns, bool head) {
     const unsigned lane = lane0();
-    if (t == 0) return init;
+    if (head) return init;
     A excl = identity;
     long long end = (long long)t - 1;
     uint64_t t_start = 0;
@@ -284,6 +291,11 @@ __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A
     }
     if (lane == 0) publish_any(st, t, kFlagPrefix, op(excl, agg));
     return excl;
+}
+template <int K, class A, class F>
+__device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
+                                                    uint32_t* status, uint64_t timeout_ns) {
+    return decoupled_lookback_any<K>(st, t, agg, init, identity, op, status, timeout_ns, t == 0);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -27,6 +27,12 @@
 
 #include <limits>
 
+// rows x cols, row r of the input at r*ld_in elements and of the output at r*ld_out (rows = 1: a
+// plain scan of cols elements; the leading dimensions are then ignored).
+struct ScanShape {
+    size_t rows, cols, ld_in, ld_out;
+};
+
 namespace {
 
 #ifndef KI_SCAN_ANY_SMALL_BATCH
@@ -47,10 +53,13 @@ struct Shape {
     static constexpr int kTile = kWorkWarps * kSpan;          // elements per tile
 };
 
+// The input is rows x cols (rows = 1 for a plain scan): row r starts ld_in elements after row r-1
+// in the input and ld_out after it in the output, and every row is a segment of its own, cut into
+// tpr tiles; tile t is chunk t % tpr of row t / tpr.
 struct AnyArgs {
     const void* in;
     void* out;
-    size_t n;
+    size_t rows, cols, ld_in, ld_out, tpr;
     uint64_t init_bits;  // init in the accumulation type, as raw bits
     ki::TileStatus st;
     unsigned long long* ticket;
@@ -93,15 +102,33 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
     const int tid = threadIdx.x;
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
-    const uint64_t ntiles = (a.n + S::kTile - 1) / S::kTile;
-    auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)S::kTile <= a.n; };
+    const uint64_t ntiles = (uint64_t)a.rows * a.tpr;
+    struct Where {
+        size_t in_off, out_off;  // element offsets of the tile's first element
+        int count;               // elements in the tile
+        bool head;               // first tile of its row
+    };
+    auto where = [&](uint64_t t) {
+        size_t row = 0, chunk = (size_t)t;
+        if (a.rows > 1) {  // (a plain scan is one row: no division)
+            row = (size_t)(t / a.tpr);
+            chunk = (size_t)(t - (uint64_t)row * a.tpr);
+        }
+        Where p;
+        p.in_off = row * a.ld_in + chunk * (size_t)S::kTile;
+        p.out_off = row * a.ld_out + chunk * (size_t)S::kTile;
+        p.count = (int)min((size_t)S::kTile, a.cols - chunk * (size_t)S::kTile);
+        p.head = chunk == 0;
+        return p;
+    };
+    auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && where(t).count == S::kTile; };
     auto fetch = [&]() {
         const unsigned long long t = atomicAdd(a.ticket, 1ull);
         ticket = t;
         if (bulk_ok(t)) {
             ki::fence_proxy_async_smem();
             ki::mbar_arrive_expect_tx(&bar, (uint32_t)kTileBytes);
-            ki::bulk_g2s_keep(sb, in + t * S::kTile, (uint32_t)kTileBytes, &bar);
+            ki::bulk_g2s_keep(sb, in + where(t).in_off, (uint32_t)kTileBytes, &bar);
         }
     };
     if (tid == 0) {
@@ -123,12 +150,14 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
         if (w == kLookWarp) {
             if (have_old) {
                 PendingAny<A>& o = slot[cur ^ 1];
-                const A ex = ki::decoupled_lookback_any<1>(a.st, o.t, o.agg, init, id, op, a.status, a.timeout_ns);
+                const A ex = ki::decoupled_lookback_any<1>(a.st, o.t, o.agg, init, id, op, a.status, a.timeout_ns,
+                                                           where(o.t).head);
                 if (lane == 0) o.tile_excl = ex;
             }
         } else if (new_valid) {
-            const size_t first = (size_t)t_new * S::kTile;
-            const int count = (int)min((size_t)S::kTile, a.n - first);
+            const Where p = where(t_new);
+            const size_t first = p.in_off;
+            const int count = p.count;
             if (bulk_ok(t_new)) {
                 if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
                     ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
@@ -160,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 if (lane == 0) {
                     e.t = t_new;
                     e.agg = agg;
-                    ki::publish_aggregate_any(a.st, t_new, agg, init, op);
+                    ki::publish_aggregate_any(a.st, t_new, agg, init, op, p.head);
                 }
             }
         }
@@ -170,8 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
         if (tid == kLookWarp * 32 && new_valid) fetch();
         if (w < kWorkWarps && have_old) {
             const PendingAny<A>& o = slot[cur ^ 1];
-            const size_t first = (size_t)o.t * S::kTile;
-            const int count = (int)min((size_t)S::kTile, a.n - first);
+            const Where p = where(o.t);
+            const size_t first = p.in_off, out_first = p.out_off;
+            const int count = p.count;
             const bool full = count == S::kTile;
             A carry = op(o.tile_excl, o.warp_excl[w]);
             const T pad = ki::pad_value<T, Op>();
@@ -222,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                                 r[p] = Tr::lower(run);
                             }
                         }
-                        __stcs(reinterpret_cast<uint4*>(out + first + i) + q, *reinterpret_cast<const uint4*>(r));
+                        __stcs(reinterpret_cast<uint4*>(out + out_first + i) + q, *reinterpret_cast<const uint4*>(r));
                     }
                 } else {
 #pragma unroll
@@ -236,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                             run = op(run, x);
                             r = Tr::lower(run);
                         }
-                        if (i + e < count) out[first + i + e] = r;
+                        if (i + e < count) out[out_first + i + e] = r;
                     }
                 }
                 carry = op(carry, __shfl_sync(0xffffffffu, inc, 31));
@@ -249,40 +279,156 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
     }
 }
 
+// Short rows (at most kShortRowBytes of input): one warp per row, 32 lanes x one 16-byte vector
+// per step (the next step's vector loaded before this one is scanned), the carry passed along the
+// row; no tile status, no lookback.
+constexpr size_t kShortRowBytes = 32768;
+constexpr int kRowThreads = 256;
+
+template <class T, class Op, bool EXCL>
+__global__ void __launch_bounds__(kRowThreads) scan_rows_warp_kernel(const T* __restrict__ in,
+                                                                     typename ki::Traits<T, Op>::R* __restrict__ out,
+                                                                     size_t rows, size_t cols, size_t ld_in,
+                                                                     size_t ld_out, uint64_t init_bits, int vec_in,
+                                                                     int vec_out) {
+    using Tr = ki::Traits<T, Op>;
+    using A = typename Tr::A;
+    using R = typename Tr::R;
+    constexpr int kE = (int)(16 / sizeof(T));
+    constexpr int kRow = 32 * kE;
+    const ki::OpFn<T, Op> op;
+    const A id = Tr::identity();
+    const A init = ki::from_bits<A>(init_bits);
+    const T pad = ki::pad_value<T, Op>();
+    const unsigned lane = threadIdx.x & 31;
+    const size_t nwarps = ((size_t)gridDim.x * kRowThreads) >> 5;
+    auto load = [&](const T* x, size_t c0) {
+        ki::Packed16<T> v;
+        const size_t i = c0 + (size_t)kE * lane;
+        if (vec_in && c0 + kRow <= cols) {
+            v.raw = __ldcs(reinterpret_cast<const uint4*>(x + i));
+        } else {
+#pragma unroll
+            for (int e = 0; e < kE; ++e) v.set(e, (i + e < cols) ? x[i + e] : pad);
+        }
+        return v;
+    };
+    for (size_t row = ((size_t)blockIdx.x * kRowThreads + threadIdx.x) >> 5; row < rows; row += nwarps) {
+        const T* x = in + row * ld_in;
+        R* y = out + row * ld_out;
+        A carry = init;
+        ki::Packed16<T> next = load(x, 0);
+        for (size_t c0 = 0; c0 < cols; c0 += kRow) {
+            const ki::Packed16<T> v = next;
+            if (c0 + kRow < cols) next = load(x, c0 + kRow);
+            A tot = Tr::lift(v.get(0));
+#pragma unroll
+            for (int e = 1; e < kE; ++e) tot = op(tot, Tr::lift(v.get(e)));
+            const A inc = ki::warpreduce(tot, op);
+            A before = __shfl_up_sync(0xffffffffu, inc, 1);
+            if (lane == 0) before = id;
+            A run = op(carry, before);
+            const size_t i = c0 + (size_t)kE * lane;
+            if (vec_out && c0 + kRow <= cols) {
+                constexpr int kPer = (int)(16 / sizeof(R));
+#pragma unroll
+                for (int q = 0; q < kE / kPer; ++q) {
+                    alignas(16) R r[kPer];
+#pragma unroll
+                    for (int p = 0; p < kPer; ++p) {
+                        const A xv = Tr::lift(v.get(q * kPer + p));
+                        if (EXCL) {
+                            r[p] = Tr::lower(run);
+                            run = op(run, xv);
+                        } else {
+                            run = op(run, xv);
+                            r[p] = Tr::lower(run);
+                        }
+                    }
+                    __stcs(reinterpret_cast<uint4*>(y + i) + q, *reinterpret_cast<const uint4*>(r));
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < kE; ++e) {
+                    const A xv = Tr::lift(v.get(e));
+                    R r;
+                    if (EXCL) {
+                        r = Tr::lower(run);
+                        run = op(run, xv);
+                    } else {
+                        run = op(run, xv);
+                        r = Tr::lower(run);
+                    }
+                    if (i + e < cols) y[i + e] = r;
+                }
+            }
+            carry = op(carry, __shfl_sync(0xffffffffu, inc, 31));
+        }
+    }
+}
+
+// init: a host value of the result type, converted to the accumulation type; else the identity.
 template <class T, class Op>
-int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, size_t n, const void* h_init, cudaStream_t s) {
+typename ki::Traits<T, Op>::A init_value(const void* h_init) {
+    using Tr = ki::Traits<T, Op>;
+    using A = typename Tr::A;
+    using R = typename Tr::R;
+    if (h_init) {
+        R r;
+        memcpy(&r, h_init, sizeof(R));
+        if constexpr (std::is_same<Op, ki::JAdd>::value || std::is_same<Op, ki::JMul>::value) return (A)r;
+        else return Tr::lift(r);
+    } else if constexpr (std::is_same<Op, ki::JAdd>::value) {
+        return A(0);
+    } else if constexpr (std::is_same<Op, ki::JMul>::value) {
+        return A(1);
+    } else if constexpr (ki::IsBitwise<Op>::value) {
+        return Tr::identity();
+    } else if constexpr (std::is_floating_point<T>::value) {
+        return Tr::lift(std::is_same<Op, ki::JMax>::value ? -std::numeric_limits<T>::infinity()
+                                                          : std::numeric_limits<T>::infinity());
+    } else {
+        return std::is_same<Op, ki::JMax>::value ? std::numeric_limits<A>::lowest() : std::numeric_limits<A>::max();
+    }
+}
+
+template <class T, class Op>
+int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, const ScanShape& sh, const void* h_init,
+                cudaStream_t s) {
     using Tr = ki::Traits<T, Op>;
     using A = typename Tr::A;
     using R = typename Tr::R;
     using S = Shape<T>;
     if (!ki::aligned(d_in, sizeof(T)) || !ki::aligned(d_out, sizeof(R)))
         return ki::set_error(ctx, KI_ERR_ARG, "scan: misaligned input or output");
+    const size_t rows = sh.rows, cols = sh.cols;
+    const size_t ld_in = rows > 1 ? sh.ld_in : cols, ld_out = rows > 1 ? sh.ld_out : cols;
     const uintptr_t i0 = (uintptr_t)d_in, o0 = (uintptr_t)d_out;
-    const uintptr_t ib = n * sizeof(T), ob = n * sizeof(R);
-    if (!(i0 == o0 && sizeof(T) == sizeof(R)) && i0 < o0 + ob && o0 < i0 + ib)
+    const uintptr_t ib = ((rows - 1) * ld_in + cols) * sizeof(T), ob = ((rows - 1) * ld_out + cols) * sizeof(R);
+    const bool in_place = i0 == o0 && sizeof(T) == sizeof(R) && ld_in == ld_out;
+    if (!in_place && i0 < o0 + ob && o0 < i0 + ib)
         return ki::set_error(ctx, KI_ERR_ARG, "scan: input and output overlap (only an exact in-place scan is allowed)");
-    // init: a host value of the result type, converted to the accumulation type; else the identity
-    A init;
-    if (h_init) {
-        R r;
-        memcpy(&r, h_init, sizeof(R));
-        if constexpr (std::is_same<Op, ki::JAdd>::value || std::is_same<Op, ki::JMul>::value) init = (A)r;
-        else init = Tr::lift(r);
-    } else if constexpr (std::is_same<Op, ki::JAdd>::value) {
-        init = A(0);
-    } else if constexpr (std::is_same<Op, ki::JMul>::value) {
-        init = A(1);
-    } else if constexpr (ki::IsBitwise<Op>::value) {
-        init = Tr::identity();
-    } else {
-        using TT = typename std::conditional<std::is_floating_point<T>::value, T, double>::type;
-        if constexpr (std::is_floating_point<T>::value)
-            init = Tr::lift(std::is_same<Op, ki::JMax>::value ? -std::numeric_limits<TT>::infinity()
-                                                               : std::numeric_limits<TT>::infinity());
+    const A init = init_value<T, Op>(h_init);
+    uint64_t init_bits = 0;
+    memcpy(&init_bits, &init, sizeof(A));
+    const int vec_in = ki::aligned(d_in, 16) && (rows == 1 || (ld_in * sizeof(T)) % 16 == 0);
+    const int vec_out = ki::aligned(d_out, 16) && (rows == 1 || (ld_out * sizeof(R)) % 16 == 0);
+    if (rows > 1 && cols * sizeof(T) <= kShortRowBytes) {
+        size_t blocks = (rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
+        const size_t cap = (size_t)ctx->sm_count * (2048 / kRowThreads);
+        if (blocks > cap) blocks = cap;
+        const T* x = static_cast<const T*>(d_in);
+        R* y = static_cast<R*>(d_out);
+        if (excl)
+            scan_rows_warp_kernel<T, Op, true><<<(unsigned)blocks, kRowThreads, 0, s>>>(x, y, rows, cols, ld_in, ld_out,
+                                                                                      init_bits, vec_in, vec_out);
         else
-            init = std::is_same<Op, ki::JMax>::value ? std::numeric_limits<A>::lowest() : std::numeric_limits<A>::max();
+            scan_rows_warp_kernel<T, Op, false><<<(unsigned)blocks, kRowThreads, 0, s>>>(x, y, rows, cols, ld_in, ld_out,
+                                                                                       init_bits, vec_in, vec_out);
+        return ki::check_launch(ctx, "scan_rows_warp_kernel launch");
     }
-    const size_t ntiles = (n + S::kTile - 1) / S::kTile;
+    const size_t tpr = (cols + S::kTile - 1) / S::kTile;
+    const size_t ntiles = rows * tpr;
     const size_t words_off = 256;
     void* base = nullptr;
     int rc = ki::ensure_region(ctx, KI_REG_SCAN_ANY, words_off + ntiles * 24, &base);
@@ -292,17 +438,20 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, size_t n,
     AnyArgs a;
     a.in = d_in;
     a.out = d_out;
-    a.n = n;
-    a.init_bits = 0;
-    memcpy(&a.init_bits, &init, sizeof(A));
+    a.rows = rows;
+    a.cols = cols;
+    a.ld_in = ld_in;
+    a.ld_out = ld_out;
+    a.tpr = tpr;
+    a.init_bits = init_bits;
     a.st.words = reinterpret_cast<uint64_t*>(b + words_off);
     a.st.aggs = reinterpret_cast<int64_t*>(b + words_off + ntiles * 8);
     a.st.incls = reinterpret_cast<int64_t*>(b + words_off + ntiles * 16);
     a.ticket = reinterpret_cast<unsigned long long*>(b);
     a.status = ctx->d_status;
     a.timeout_ns = ctx->wait_timeout_ns;
-    a.tma_in = ki::aligned(d_in, 16);
-    a.vec_out = ki::aligned(d_out, 16);
+    a.tma_in = vec_in;
+    a.vec_out = vec_out;
     size_t grid = (size_t)ctx->sm_count;
     if (grid > ntiles) grid = ntiles;
     if (excl) {
@@ -318,12 +467,12 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, size_t n,
 }
 
 template <class Op>
-int scan_op(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, size_t n, const void* h_init,
+int scan_op(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, const ScanShape& sh, const void* h_init,
             cudaStream_t s) {
     constexpr int kBad = -1000;
     const int rc = ki::with_dtype(dtype, kBad, [&](auto tag) -> int {
         using T = decltype(tag);
-        if constexpr (ki::op_takes<T, Op>()) return scan_launch<T, Op>(ctx, excl, d_in, d_out, n, h_init, s);
+        if constexpr (ki::op_takes<T, Op>()) return scan_launch<T, Op>(ctx, excl, d_in, d_out, sh, h_init, s);
         else return kBad;
     });
     if (rc == kBad) return ki::set_error(ctx, KI_ERR_ARG, "scan: the operator does not take this element type");
@@ -333,8 +482,9 @@ int scan_op(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, si
 }  // namespace
 
 // One per operator, defined in scan_any*.cu.
-#define KI_SCAN_ANY_ENTRY(name) \
-    __attribute__((visibility("hidden"))) int name(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, size_t n, const void* h_init, cudaStream_t s)
+#define KI_SCAN_ANY_ENTRY(name)                                                                                \
+    __attribute__((visibility("hidden"))) int name(ki_ctx* ctx, int dtype, bool excl, const void* d_in, void* d_out, \
+                                                   const ScanShape& sh, const void* h_init, cudaStream_t s)
 KI_SCAN_ANY_ENTRY(ki_scan_any_add);
 KI_SCAN_ANY_ENTRY(ki_scan_any_mul);
 KI_SCAN_ANY_ENTRY(ki_scan_any_max);

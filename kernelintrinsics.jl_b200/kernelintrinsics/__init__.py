@@ -622,6 +622,32 @@ def scan(x, op: str = "+", exclusive: bool = False, init=None, out=None, stream=
     return out
 
 
+def scan_rows(x, op: str = "+", exclusive: bool = False, init=None, out=None, stream=None):
+    """accumulate(op, x; dims) along each row of a 2-D ``x`` whose rows are contiguous
+    (``x.stride(1) == 1``; ``x.stride(0)`` is the leading dimension), every row starting from ``init``.
+    Operators and result types as ``scan``; ``out`` (rows contiguous) may have its own row stride."""
+    import numpy as np
+
+    torch = _torch()
+    d = _dev(x)
+    if op not in _GENERIC_OPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"scan_rows: op must be one of {sorted(_GENERIC_OPS)}")
+    if x.dim() != 2 or (x.shape[1] > 1 and x.stride(1) != 1):
+        raise KIArgumentError(_abi.KI_ERR_ARG, "scan_rows: 2-D input with contiguous rows")
+    rows, cols = x.shape
+    rd = _result_dtype(x.dtype, op)
+    out = torch.empty((rows, cols), dtype=rd, device=x.device) if out is None else out
+    if out.shape != x.shape or out.dtype != rd or (cols > 1 and out.stride(1) != 1):
+        raise KIArgumentError(_abi.KI_ERR_ARG, "scan_rows: output of the input's shape, result type and contiguous rows")
+    init_buf = None if init is None else np.array([init], dtype=_np_dtype(rd))
+    ld_in = x.stride(0) if rows > 1 else cols
+    ld_out = out.stride(0) if rows > 1 else cols
+    context(d).call("ki_scan_rows", _GENERIC_OPS[op], _dtype_code(x), int(bool(exclusive)), _ptr(x), max(ld_in, cols),
+                    _ptr(out), max(ld_out, cols), rows, cols,
+                    ctypes.c_void_p(init_buf.ctypes.data) if init_buf is not None else None, _stream_ptr(stream, d))
+    return out
+
+
 _PREDS = {">": 0, ">=": 1, "<": 2, "<=": 3, "==": 4, "!=": 5}
 
 

@@ -213,3 +213,48 @@ def test_reduce_rows_empty_rows(KI, dev):
     for op in ("max", "|"):
         with pytest.raises(KI.KIArgumentError):
             KI.reduce_rows(torch.empty((4, 0), dtype=torch.int32, device=dev), op)
+
+
+SCAN_ROW_SHAPES = [(1, 5), (3, 1), (7, 33), (1000, 100), (300, 2049), (5, 8192), (40, 9000), (3, 100_003), (2, 400_001)]
+
+
+@pytest.mark.parametrize("dt,op", [c for c in _cases() if c.values[1] == "+" or c.values[0] in (np.int8, np.int32, np.float64)])
+def test_scan_rows(KI, oracle, dev, dt, op):
+    """Segmented scan (accumulate along each row): short rows (one warp per row) and long rows (tiles
+    with a lookback segment per row), padded rows (ld > cols), unaligned starts, exclusive with init."""
+    import torch
+
+    for k, (rows, cols) in enumerate(SCAN_ROW_SHAPES):
+        for pad, excl in ((0, False), (3, True)):
+            ld = cols + pad
+            flat = _data(dt, rows * ld + 1, 2000 + k, op)
+            m = flat[1:].reshape(rows, ld) if pad else flat[: rows * ld].reshape(rows, ld)
+            xd = _to_dev(flat, dev)
+            view = (xd[1:] if pad else xd[: rows * ld]).view(rows, ld)[:, :cols]
+            init = None if not excl else (3 if np.dtype(dt).kind != "f" else 0.5)
+            got = KI.scan_rows(view, op, exclusive=excl, init=init).cpu().numpy()
+            for r in range(rows) if rows <= 40 else range(0, rows, max(1, rows // 40)):
+                want = oracle.accumulate(op, m[r, :cols], init=init, exclusive=excl)
+                x = m[r, :cols] if not excl else np.concatenate([[0], m[r, :cols][:-1]]).astype(m.dtype)
+                _check(got[r], want, x, op)
+    KI.context(0).check()
+
+
+def test_scan_rows_strided_output_and_in_place(KI, oracle, dev):
+    import torch
+
+    x = _data(np.int64, 64 * 5000, 77, "+").reshape(64, 5000)
+    xd = _to_dev(x, dev)
+    out = torch.zeros(64, 5008, dtype=torch.int64, device=dev)
+    KI.scan_rows(xd, "+", out=out[:, 3:5003])
+    got = out.cpu().numpy()
+    for r in range(64):
+        assert np.array_equal(got[r, 3:5003], oracle.accumulate("+", x[r]))
+    assert not got[:, :3].any() and not got[:, 5003:].any()
+    y = xd.clone()
+    KI.scan_rows(y, "max", out=y)
+    for r in range(0, 64, 7):
+        assert np.array_equal(y[r].cpu().numpy(), oracle.accumulate("max", x[r]))
+    with pytest.raises(KI.KIArgumentError):  # rows overlapping another layout
+        KI.scan_rows(xd[:, :4000], "+", out=xd[:, 1000:])
+    KI.context(0).check()

@@ -136,6 +136,13 @@ int ki_reduce_sum_i64(ki_ctx* ctx, const int64_t* d_x, size_t n, int64_t* d_out,
  * writes zero, KI_OP_MUL one, the others return KI_ERR_ARG (Base throws on an empty maximum).
  * Deterministic for a given n and device. */
 int ki_reduce(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t n, void* d_out, void* stream);
+/* Element maps applied before a fold or a predicate, in the element type as Base computes them
+ * (abs(typemin(Int8)) == typemin(Int8); abs2 wraps on integers; abs is the identity on unsigned). */
+typedef enum { KI_MAP_IDENTITY = 0, KI_MAP_ABS = 1, KI_MAP_ABS2 = 2 } ki_map;
+/* mapreduce(f, op, x): Base.sum(abs2, x), maximum(abs, x) and the like.  With KI_MAP_IDENTITY it is
+ * ki_reduce; with KI_MAP_ABS or KI_MAP_ABS2 op is KI_OP_ADD, KI_OP_MAX or KI_OP_MIN, the result type
+ * that of ki_reduce for (op, dtype), and the map runs in the element type before the widening. */
+int ki_mapreduce(ki_ctx* ctx, int map, int op, int dtype, const void* d_x, size_t n, void* d_out, void* stream);
 /* Segmented reduce: one ki_reduce per row of a row-major rows x cols matrix whose rows start ld
  * elements apart (ld >= cols; a column-major Julia matrix reduced along dims=1 has rows = its
  * columns).  d_out receives rows values of ki_reduce's result type.  cols = 0: KI_OP_ADD writes
@@ -199,6 +206,12 @@ int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float threshold, 
 typedef enum { KI_PRED_GT = 0, KI_PRED_GE = 1, KI_PRED_LT = 2, KI_PRED_LE = 3, KI_PRED_EQ = 4, KI_PRED_NE = 5 } ki_pred;
 int ki_compact(ki_ctx* ctx, int pred, int dtype, const void* d_x, size_t n, const void* h_thr, void* d_out_vals,
                int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream);
+/* Fused map-then-compact: keeps x[i] with map(x[i]) pred threshold (filter(v -> abs(v) > t, x) and
+ * its findall); the kept elements are written as they are, not mapped.  map: a ki_map (with
+ * KI_MAP_IDENTITY it is ki_compact); the threshold is compared with the mapped value in the element
+ * type.  Null d_out_vals and d_out_idx give count(v -> map(v) pred t, x) in d_count. */
+int ki_compact_map(ki_ctx* ctx, int map, int pred, int dtype, const void* d_x, size_t n, const void* h_thr,
+                   void* d_out_vals, int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream);
 
 /* ---- (a8) fp8 e4m3 GEMM on tcgen05 / TMEM ---------------------------------------------------
  * No counterpart in the reference.  C = (scale_a * scale_b) * A * B with A: M x K row-major e4m3,

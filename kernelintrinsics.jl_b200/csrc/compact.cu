@@ -1,374 +1,5 @@
-// compact.cu -- order-preserving stream compaction: filter(v -> v op t, x) and findall(v -> v op t, x)
-// for op in >, >=, <, <=, ==, != over Int32, UInt32, Int64, UInt64, Float32 and Float64 (IEEE
-// comparisons, as Base's operators).
-//
-// Persistent CTAs (3 per SM), software-pipelined over 64 KiB tiles (16384 4-byte or 8192 8-byte
-// elements; the description below counts 4-byte elements), with 8 "work" warps
-// and one "look" warp, the same pipeline as scan.cu.  Iteration k of a CTA runs two phases:
-//   phase A  work warps: wait for tile k (one 64 KiB 1-D TMA bulk copy, cp.async.bulk ...
-//            mbarrier::complete_tx) and count its kept elements (warp w owns 2048 elements as 16 rows
-//            of 32 lanes x float4: conflict-free 16-byte shared loads); warp 0 scans the 8 warp
-//            counts with @warpreduce and publishes the tile count at once (ki/lookback.cuh);
-//            look warp, at the same time: an L2 bulk prefetch of tile k-1 (cp.async.bulk.prefetch)
-//            and the decoupled lookback of tile k-1;
-//   phase B  the look warp takes the next ticket and starts its TMA into the free buffer;
-//            work warps write tile k-1: re-read it from global memory (L2) and, for each row and
-//            component c, take a @vote Ballot (ext/CUDA/shuffle_vote.jl:23-34, vote.sync ballot ->
-//            UInt32).  An element's rank inside its row is
-//                sum over c of popc(ballot_c & lanes_below) + (kept components before it in its lane)
-//            which keeps source order (lane-major, then component).  The row's kept values and
-//            indices go to a per-warp shared-memory run at their ranks (an element that is not kept
-//            goes to its lane's discard slot, so there are no branches) and leave as coalesced
-//            evict-first stores at tile prefix + warp prefix + row prefix.
-// Between taking a ticket and publishing that tile's count a CTA only waits for its own load and
-// its own second pass, never for a lookback.  Tiles that are not 16-byte aligned are read with plain
-// loads; in the partial last tile, elements past the end are excluded explicitly.
-//
-// Measured at n = 2^28 (0.467 ms, 0.57 of the copy peak): without the stores the same kernel takes
-// 0.235 ms.  Writing the output streams evicts tiles that wait for their prefix, so most second-pass
-// reads come back from DRAM; the prefetch turns them into one asynchronous bulk read per tile
-// (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read (also
-// with the lines demoted to normal priority after the second read: 0.48 ms), evict-first second
-// reads (0.50), tiles kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-
-// element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
-// per SM of 16 warps over 64 KiB tiles (0.48), looking tile k up right after its count, early
-// tickets.  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
-#include "ki/common.cuh"
-#include "ki/intrinsics.cuh"
-#include "ki/lookback.cuh"
-#include "ki/ops.cuh"
-
-namespace {
-
-#ifndef KI_COMPACT_LOOKBACK_K
-#define KI_COMPACT_LOOKBACK_K 1
-#endif
-#ifndef KI_COMPACT_PREFETCH
-#define KI_COMPACT_PREFETCH 1
-#endif
-#ifndef KI_COMPACT_CTAS_PER_SM
-#define KI_COMPACT_CTAS_PER_SM 3
-#endif
-#ifndef KI_COMPACT_WORK_WARPS
-#define KI_COMPACT_WORK_WARPS 8
-#endif
-#ifndef KI_COMPACT_ROWS
-#define KI_COMPACT_ROWS 16
-#endif
-constexpr int kWorkWarps = KI_COMPACT_WORK_WARPS;
-constexpr int kLookWarp = kWorkWarps;
-constexpr int kWorkThreads = 32 * kWorkWarps;
-constexpr int kThreads = kWorkThreads + 32;
-constexpr int kRows = KI_COMPACT_ROWS;  // rows of 32 lanes x one 16-byte vector per work warp
-constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 512;  // 64 KiB: 16384 elements of 4 bytes or 8192 of 8
-constexpr int kBatch = 8;             // rows loaded at once in the second pass
-constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
-constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
-
-template <class T>
-struct CShape {
-    static constexpr int kE = (int)(16 / sizeof(T));         // elements per lane per row
-    static constexpr int kRow = 32 * kE;                      // elements per row
-    static constexpr int kSpan = kRows * kRow;                 // elements per work warp
-    static constexpr int kTile = kWorkWarps * kSpan;           // elements per tile
-    static constexpr int kStageSlots = kRow + 32;              // a row's run + one discard slot per lane
-    static constexpr size_t kStageBytes = (size_t)kWorkWarps * kStageSlots * (sizeof(T) + sizeof(int32_t));
-    static constexpr size_t kSmemBytes = kTileBytes + kStageBytes;
-    static_assert(kTile * sizeof(T) == kTileBytes, "tile layout");
-};
-
-// Comparison predicates (x op t), IEEE semantics for floats as Base's <, <=, ==, != and >.
-struct PGt { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x > t; } };
-struct PGe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x >= t; } };
-struct PLt { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x < t; } };
-struct PLe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x <= t; } };
-struct PEq { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x == t; } };
-struct PNe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x != t; } };
-
-struct CompactArgs {
-    const void* x;
-    size_t n;
-    uint64_t thr_bits;  // the threshold, as a T
-    void* out_vals;
-    int32_t* out_idx;
-    int64_t index_base;
-    uint64_t* d_count;
-    ki::TileStatus st;
-    unsigned long long* ticket;
-    uint32_t* status;
-    uint64_t timeout_ns;
-    int tma_in;  // x is 16-byte aligned: full tiles come in by TMA, rows as 16-byte vectors
-};
-
-struct Pending {
-    unsigned long long t;
-    int64_t agg;
-    int64_t tile_excl;
-    int warp_excl[kWorkWarps];
-};
-
-__device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
-
-// T: element type; P: predicate; VALS / IDX: which outputs are written (an absent output costs no
-// instructions).
-template <class T, class P, bool VALS, bool IDX>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactArgs a) {
-    using S = CShape<T>;
-    using V = ki::Vec16<T>;
-    constexpr int kE = S::kE;
-    constexpr int kTile = S::kTile;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    T* sb = reinterpret_cast<T*>(smem_raw);
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ int warp_cnt[kWorkWarps];
-    __shared__ Pending slot[2];  // tile k (being counted) and tile k-1 (being written)
-    __shared__ unsigned long long ticket;
-
-    const T* x = static_cast<const T*>(a.x);
-    const T thr = ki::from_bits<T>(a.thr_bits);
-    const int tid = threadIdx.x;
-    const int w = tid >> 5;
-    const unsigned lane = tid & 31;
-    const uint64_t ntiles = (a.n + kTile - 1) / kTile;
-    auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
-    auto fetch = [&]() {  // take a ticket and start its load (one thread)
-        const unsigned long long t = atomicAdd(a.ticket, 1ull);
-        ticket = t;
-        if (bulk_ok(t)) {
-            ki::fence_proxy_async_smem();  // earlier generic reads of sb come first
-            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kTileBytes);
-            ki::bulk_g2s(sb, x + t * kTile, (uint32_t)kTileBytes, &bar);
-        }
-    };
-    if (tid == 0) {
-        ki::mbar_init(&bar, 1);
-        ki::fence_mbar_init();
-        fetch();
-    }
-    __syncthreads();
-
-    const unsigned below = (1u << lane) - 1u;  // lanes with a lower index
-    uint32_t phase = 0;
-    bool have_old = false;
-    int cur = 0;  // slot of tile k; tile k-1 is in slot cur ^ 1
-    while (true) {
-        const uint64_t t_new = ticket;
-        const bool new_valid = t_new < ntiles;
-        if (!new_valid && !have_old) break;
-
-        // ---- phase A: count and publish tile k  ||  prefetch and look back for tile k-1 ------------
-        if (w == kLookWarp) {
-            if (have_old) {
-                Pending& o = slot[cur ^ 1];
-                // bring tile k-1 back into L2 (if it left) while its prefix is looked up
-                if (KI_COMPACT_PREFETCH && lane == 0 && bulk_ok(o.t))
-                    ki::bulk_prefetch_l2(x + o.t * kTile, (uint32_t)kTileBytes);
-                const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, 0, a.status, a.timeout_ns);
-                if (lane == 0) o.tile_excl = ex;
-            }
-        } else if (new_valid) {
-            const size_t first = (size_t)t_new * kTile;
-            const int count = (int)min((size_t)kTile, a.n - first);
-            if (bulk_ok(t_new)) {
-                if (!ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns))
-                    ki::mbar_wait_bounded(&bar, phase, a.status, a.timeout_ns);  // never leave a copy in flight
-                phase ^= 1u;
-            } else {
-                for (int i = tid; i < kTile; i += kWorkThreads) sb[i] = (i < count) ? x[first + i] : T(0);
-                work_sync();
-            }
-            const V* row0 = reinterpret_cast<const V*>(sb + w * S::kSpan) + lane;
-            int c = 0;
-            if (count == kTile) {
-#pragma unroll 8
-                for (int j = 0; j < kRows; ++j) {
-                    const V v = row0[32 * j];
-#pragma unroll
-                    for (int e = 0; e < kE; ++e) c += P::test(v.v[e], thr);
-                }
-            } else {  // the partial last tile: elements past count do not exist
-                const int i_lane = w * S::kSpan + kE * (int)lane;
-                for (int j = 0; j < kRows; ++j) {
-                    const V v = row0[32 * j];
-#pragma unroll
-                    for (int e = 0; e < kE; ++e) c += (i_lane + S::kRow * j + e < count) && P::test(v.v[e], thr);
-                }
-            }
-            c = ki::warpfold(c, ki::Add{});
-            if (lane == 0) warp_cnt[w] = c;
-            work_sync();
-            if (w == 0) {
-                const int xx = (lane < (unsigned)kWorkWarps) ? warp_cnt[lane] : 0;
-                const int inc = ki::warpreduce(xx, ki::Add{});
-                const int agg = __shfl_sync(0xffffffffu, inc, kWorkWarps - 1);
-                Pending& e = slot[cur];
-                if (lane < (unsigned)kWorkWarps) e.warp_excl[lane] = inc - xx;
-                if (lane == 0) {
-                    e.t = t_new;
-                    e.agg = agg;
-                    ki::publish_aggregate(a.st, t_new, agg, 0);
-                }
-            }
-        }
-        __syncthreads();  // tile k counted (buffer free, slot written); tile k-1's prefix known
-
-        // ---- phase B: start tile k+1's load; write tile k-1 -------------------------------------------
-        if (tid == kLookWarp * 32 && new_valid) fetch();  // the look warp is idle in phase B
-        if (w < kWorkWarps && have_old) {
-            const Pending& o = slot[cur ^ 1];
-            const size_t first = (size_t)o.t * kTile;
-            const int count = (int)min((size_t)kTile, a.n - first);
-            const bool full = count == kTile;
-            const bool vec_in = a.tma_in;
-            // outputs of this warp start at one pointer; offsets from it fit 32 bits
-            const int64_t at = o.tile_excl + o.warp_excl[w];
-            T* vals = VALS ? static_cast<T*>(a.out_vals) + at : nullptr;
-            int32_t* idxs = IDX ? a.out_idx + at : nullptr;
-            const int i_lane = w * S::kSpan + kE * (int)lane;  // element of (row 0, component 0)
-            // output index of that element; unsigned, so indices past the last element wrap
-            // harmlessly instead of overflowing (they are never stored)
-            const uint32_t ix0 = (uint32_t)((int64_t)first + a.index_base) + (uint32_t)i_lane;
-            T* sv = reinterpret_cast<T*>(smem_raw + kTileBytes) + (size_t)w * S::kStageSlots;
-            int32_t* si = reinterpret_cast<int32_t*>(smem_raw + kTileBytes + (size_t)kWorkWarps * S::kStageSlots * sizeof(T)) +
-                          (size_t)w * S::kStageSlots;
-            int pos = 0;
-            // FULL: a whole tile (no element past the end), the common case, without bounds checks
-            auto rows_pass = [&](auto full_tag) {
-                constexpr bool FULL = decltype(full_tag)::value;
-#pragma unroll 1
-                for (int j0 = 0; j0 < kRows; j0 += kBatch) {
-                    V v[kBatch];
-#pragma unroll
-                    for (int j = 0; j < kBatch; ++j) {  // a batch of loads in flight first
-                        const int i0 = i_lane + S::kRow * (j0 + j);
-                        if (FULL && vec_in) {
-                            const uint4 raw = *reinterpret_cast<const uint4*>(x + first + i0);
-                            v[j] = *reinterpret_cast<const V*>(&raw);
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < kE; ++e) v[j].v[e] = (FULL || i0 + e < count) ? x[first + i0 + e] : T(0);
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < kBatch; ++j) {
-                        const int i0 = i_lane + S::kRow * (j0 + j);
-                        bool p[kE];
-                        unsigned b[kE];
-                        int ahead = 0, row = 0;
-#pragma unroll
-                        for (int e = 0; e < kE; ++e) {
-                            p[e] = P::test(v[j].v[e], thr);
-                            if (!FULL) p[e] = p[e] && (i0 + e < count);
-                            b[e] = ki::ballot(p[e]);
-                            ahead += __popc(b[e] & below);
-                            row += __popc(b[e]);
-                        }
-                        const uint32_t ix = ix0 + (uint32_t)(S::kRow * (j0 + j));
-                        // the row's kept elements, in source order, as one run in this warp's stage
-                        // (an element that is not kept goes to the lane's discard slot: no branches) ...
-                        const int junk = S::kRow + (int)lane;
-                        int r = ahead;
-#pragma unroll
-                        for (int e = 0; e < kE; ++e) {
-                            const int at_e = p[e] ? r : junk;
-                            if (VALS) sv[at_e] = v[j].v[e];
-                            if (IDX) si[at_e] = (int32_t)(ix + (uint32_t)e);
-                            r += (int)p[e];
-                        }
-                        __syncwarp();
-                        // ... written out with consecutive lanes on consecutive addresses
-                        for (int q = (int)lane; q < row; q += 32) {
-                            if (VALS) __stcs(vals + pos + q, sv[q]);
-                            if (IDX) __stcs(idxs + pos + q, si[q]);
-                        }
-                        __syncwarp();
-                        pos += row;
-                    }
-                }
-            };
-            if (full) rows_pass(std::true_type{});
-            else rows_pass(std::false_type{});
-            if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);
-        }
-        __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free
-        have_old = new_valid;
-        cur ^= 1;
-    }
-}
-
-template <class T, class P, bool VALS, bool IDX>
-int launch_compact(ki_ctx* ctx, const CompactArgs& a, size_t grid, cudaStream_t s) {
-    constexpr size_t smem = CShape<T>::kSmemBytes;
-    KI_CUDA(ctx, cudaFuncSetAttribute(compact_kernel<T, P, VALS, IDX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
-    compact_kernel<T, P, VALS, IDX><<<(unsigned)grid, kThreads, smem, s>>>(a);
-    return ki::check_launch(ctx, "compact_kernel launch");
-}
-
-template <class T, class P>
-int compact_run(ki_ctx* ctx, const void* d_x, size_t n, const void* h_thr, void* d_out_vals, int32_t* d_out_idx,
-                int64_t index_base, uint64_t* d_count, cudaStream_t s) {
-    constexpr int kTile = CShape<T>::kTile;
-    if (n > 0 && !ki::aligned(d_x, sizeof(T))) return ki::set_error(ctx, KI_ERR_ARG, "compact: misaligned input");
-    if ((d_out_vals && !ki::aligned(d_out_vals, sizeof(T))) || (d_out_idx && !ki::aligned(d_out_idx, 4)))
-        return ki::set_error(ctx, KI_ERR_ARG, "compact: misaligned output");
-    if (n == 0) {
-        if (d_count) KI_CUDA(ctx, cudaMemsetAsync(d_count, 0, sizeof(uint64_t), s));
-        return KI_OK;
-    }
-    const size_t ntiles = (n + kTile - 1) / kTile;
-    const size_t words_off = 256;
-    void* base = nullptr;
-    int rc = ki::ensure_region(ctx, KI_REG_COMPACT, words_off + ntiles * 24, &base);
-    if (rc) return rc;
-    char* b = static_cast<char*>(base);
-    KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * sizeof(uint64_t), s));
-    CompactArgs a;
-    a.x = d_x;
-    a.n = n;
-    a.thr_bits = 0;
-    memcpy(&a.thr_bits, h_thr, sizeof(T));
-    a.out_vals = d_out_vals;
-    a.out_idx = d_out_idx;
-    a.index_base = index_base;
-    a.d_count = d_count;
-    a.st.words = reinterpret_cast<uint64_t*>(b + words_off);
-    a.st.aggs = reinterpret_cast<int64_t*>(b + words_off + ntiles * 8);
-    a.st.incls = reinterpret_cast<int64_t*>(b + words_off + ntiles * 16);
-    a.ticket = reinterpret_cast<unsigned long long*>(b);
-    a.status = ctx->d_status;
-    a.timeout_ns = ctx->wait_timeout_ns;
-    a.tma_in = ki::aligned(d_x, 16);
-    size_t grid = (size_t)ctx->sm_count * kCtasPerSm;
-    if (grid > ntiles) grid = ntiles;
-    if (d_out_vals && d_out_idx) return launch_compact<T, P, true, true>(ctx, a, grid, s);
-    if (d_out_vals) return launch_compact<T, P, true, false>(ctx, a, grid, s);
-    if (d_out_idx) return launch_compact<T, P, false, true>(ctx, a, grid, s);
-    return launch_compact<T, P, false, false>(ctx, a, grid, s);
-}
-
-template <class T>
-int compact_pred(ki_ctx* ctx, int pred, const void* d_x, size_t n, const void* h_thr, void* d_out_vals,
-                 int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, cudaStream_t s) {
-    switch (pred) {
-        case KI_PRED_GT: return compact_run<T, PGt>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_PRED_GE: return compact_run<T, PGe>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_PRED_LT: return compact_run<T, PLt>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_PRED_LE: return compact_run<T, PLe>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_PRED_EQ: return compact_run<T, PEq>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_PRED_NE: return compact_run<T, PNe>(ctx, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        default: return ki::set_error(ctx, KI_ERR_ARG, "compact: unknown predicate");
-    }
-}
-
-int check_common(ki_ctx* ctx, const void* d_x, size_t n, int64_t index_base) {
-    if (n > 0 && !d_x) return ki::set_error(ctx, KI_ERR_ARG, "compact: null input");
-    if (index_base < INT32_MIN || (n > 0 && index_base + (int64_t)n - 1 > (int64_t)INT32_MAX))
-        return ki::set_error(ctx, KI_ERR_ARG, "compact: indices do not fit Int32");
-    return KI_OK;
-}
-
-}  // namespace
+// compact.cu -- ki_compact_gt_f32, ki_compact and ki_compact_map (kernel in compact.cuh).
+#include "compact.cuh"
 
 extern "C" int ki_compact_gt_f32(ki_ctx* ctx, const float* d_x, size_t n, float threshold, float* d_out_vals,
                                  int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream) {
@@ -388,13 +19,19 @@ extern "C" int ki_compact(ki_ctx* ctx, int pred, int dtype, const void* d_x, siz
     if (rc) return rc;
     KI_GUARD(ctx);
     cudaStream_t s = ki::as_stream(stream);
-    switch (dtype) {
-        case KI_I32: return compact_pred<int32_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_U32: return compact_pred<uint32_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_I64: return compact_pred<int64_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_U64: return compact_pred<uint64_t>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_F32: return compact_pred<float>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        case KI_F64: return compact_pred<double>(ctx, pred, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
-        default: return ki::set_error(ctx, KI_ERR_ARG, "compact: dtype must be Int32/UInt32/Int64/UInt64/Float32/Float64");
-    }
+    return compact_dtype(ctx, pred, dtype, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, s);
+}
+
+extern "C" int ki_compact_map(ki_ctx* ctx, int map, int pred, int dtype, const void* d_x, size_t n, const void* h_thr,
+                              void* d_out_vals, int32_t* d_out_idx, int64_t index_base, uint64_t* d_count,
+                              void* stream) {
+    if (map == KI_MAP_IDENTITY)
+        return ki_compact(ctx, pred, dtype, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count, stream);
+    KI_CHECK_CTX(ctx);
+    if (!h_thr) return ki::set_error(ctx, KI_ERR_ARG, "compact: null threshold");
+    int rc = check_common(ctx, d_x, n, index_base);
+    if (rc) return rc;
+    KI_GUARD(ctx);
+    return ki_compact_mapped(ctx, map, pred, dtype, d_x, n, h_thr, d_out_vals, d_out_idx, index_base, d_count,
+                             ki::as_stream(stream));
 }

@@ -94,7 +94,10 @@ struct Traits<T, JAdd> {
 
 template <class T>
 __device__ __forceinline__ T jmul(T a, T b) {
-    if constexpr (std::is_integral<T>::value) {
+    if constexpr (std::is_integral<T>::value && sizeof(T) < 4) {  // no promotion to a signed int
+        using U = typename std::make_unsigned<T>::type;
+        return (T)(U)((uint32_t)(U)a * (uint32_t)(U)b);
+    } else if constexpr (std::is_integral<T>::value) {
         using U = typename std::make_unsigned<T>::type;
         return (T)((U)a * (U)b);
     } else {
@@ -203,6 +206,38 @@ template <class T, class Op>
 struct OpFn {
     using A = typename Traits<T, Op>::A;
     __device__ __forceinline__ A operator()(A a, A b) const { return Traits<T, Op>::op(a, b); }
+};
+
+// Element maps applied before a fold or a predicate (mapreduce(f, op, x), filter(v -> f(v) > t, x)),
+// in the element type as Base computes them: abs wraps at the lowest signed value
+// (abs(typemin(Int8)) == typemin(Int8)) and is the identity on unsigned types; abs2 is x*x with
+// integer wrap-around; float abs clears the sign bit.
+struct MapId {
+    template <class T>
+    __device__ static __forceinline__ T apply(T x) { return x; }
+};
+struct MapAbs {
+    template <class T>
+    __device__ static __forceinline__ T apply(T x) {
+        if constexpr (std::is_floating_point<T>::value) return fabs(x);
+        else if constexpr (std::is_unsigned<T>::value) return x;
+        else if constexpr (sizeof(T) < 4) {
+            // |x| in 32 bits, then truncated to T (which wraps typemin back to itself, as Base's abs
+            // does).  Written as a 16-bit abs, the compiler returned +32768 for Int16 -32768 once the
+            // value was widened for the sum; the 32-bit abs goes through inline PTX so that the
+            // truncation is kept.
+            int32_t a;
+            asm("abs.s32 %0, %1;" : "=r"(a) : "r"((int32_t)x));
+            return (T)a;
+        } else {
+            using U = typename std::make_unsigned<T>::type;
+            return x < 0 ? (T)(U)(U(0) - (U)x) : x;
+        }
+    }
+};
+struct MapAbs2 {
+    template <class T>
+    __device__ static __forceinline__ T apply(T x) { return jmul(x, x); }
 };
 
 // The identity of Op as an element of T (what pads a partial tile).

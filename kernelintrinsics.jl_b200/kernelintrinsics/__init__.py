@@ -585,6 +585,25 @@ def reduce(x, op: str = "+", out=None, stream=None):
     return out
 
 
+_MAPS = {None: 0, "identity": 0, "abs": 1, "abs2": 2}
+
+
+def mapreduce(f, op: str, x, out=None, stream=None):
+    """mapreduce(f, op, x) for f in abs, abs2 (computed in the element type, as Base does) and op in
+    +, max, min: sum(abs2, x), maximum(abs, x).  Result types as ``reduce``."""
+    torch = _torch()
+    d = _dev(x)
+    if f not in _MAPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, "mapreduce: f must be 'abs', 'abs2' or None")
+    if op not in _GENERIC_OPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, f"mapreduce: op must be one of {sorted(_GENERIC_OPS)}")
+    x = x.contiguous()
+    out = torch.empty((), dtype=_result_dtype(x.dtype, op), device=x.device) if out is None else out
+    context(d).call("ki_mapreduce", _MAPS[f], _GENERIC_OPS[op], _dtype_code(x), _ptr(x), x.numel(), _ptr(out),
+                    _stream_ptr(stream, d))
+    return out
+
+
 def reduce_rows(x, op: str = "+", out=None, stream=None):
     """One reduction per row (the operators of ``reduce``) of a 2-D ``x`` whose rows are contiguous
     (``x.stride(1) == 1``; ``x.stride(0)`` is the leading dimension).  Result types as ``reduce``."""
@@ -652,31 +671,47 @@ _PREDS = {">": 0, ">=": 1, "<": 2, "<=": 3, "==": 4, "!=": 5}
 
 
 def compact(x, pred: str, threshold, out_vals=None, out_idx=None, count=None, index_base: int = 1, stream=None,
-            trim: bool = True):
-    """filter(v -> v pred threshold, x) and findall for Int32/UInt32/Int64/UInt64/Float32/Float64 ``x``
-    (IEEE comparisons).  Returns (vals, idx, count) like ``vote_compact``."""
+            trim: bool = True, f=None):
+    """filter(v -> f(v) pred threshold, x) and findall for Int32/UInt32/Int64/UInt64/Float32/Float64 ``x``
+    (IEEE comparisons; f None, 'abs' or 'abs2', applied in the element type; the kept elements are
+    x's own).  Returns (vals, idx, count) like ``vote_compact``."""
     import numpy as np
 
     torch = _torch()
     d = _dev(x)
     if pred not in _PREDS:
         raise KIArgumentError(_abi.KI_ERR_ARG, f"compact: pred must be one of {sorted(_PREDS)}")
+    if f not in _MAPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, "compact: f must be 'abs', 'abs2' or None")
     x = x.contiguous()
     n = x.numel()
-    np_dt = {torch.int32: np.int32, torch.uint32: np.uint32, torch.int64: np.int64, torch.uint64: np.uint64,
-             torch.float32: np.float32, torch.float64: np.float64}.get(x.dtype)
-    if np_dt is None:
-        raise KIArgumentError(_abi.KI_ERR_ARG, f"compact: unsupported dtype {x.dtype}")
-    thr = np.array([threshold], dtype=np_dt)
+    thr = np.array([threshold], dtype=_np_dtype(x.dtype))
     out_vals = torch.empty(n, dtype=x.dtype, device=x.device) if out_vals is None else out_vals
     out_idx = torch.empty(n, dtype=torch.int32, device=x.device) if out_idx is None else out_idx
     count = torch.zeros((), dtype=torch.uint64, device=x.device) if count is None else count
-    context(d).call("ki_compact", _PREDS[pred], _dtype_code(x), _ptr(x), n, ctypes.c_void_p(thr.ctypes.data),
+    context(d).call("ki_compact_map", _MAPS[f], _PREDS[pred], _dtype_code(x), _ptr(x), n, ctypes.c_void_p(thr.ctypes.data),
                     _ptr(out_vals), _ptr(out_idx), ctypes.c_int64(int(index_base)), _ptr(count), _stream_ptr(stream, d))
     if trim:
         k = int(count.item())
         return out_vals[:k], out_idx[:k], count
     return out_vals, out_idx, count
+
+
+def count(x, pred: str, threshold, f=None, out=None, stream=None):
+    """count(v -> f(v) pred threshold, x): the compaction pipeline with no outputs.  Returns a UInt64
+    device scalar."""
+    import numpy as np
+
+    torch = _torch()
+    d = _dev(x)
+    if pred not in _PREDS or f not in _MAPS:
+        raise KIArgumentError(_abi.KI_ERR_ARG, "count: unknown predicate or map")
+    x = x.contiguous()
+    thr = np.array([threshold], dtype=_np_dtype(x.dtype))
+    out = torch.zeros((), dtype=torch.uint64, device=x.device) if out is None else out
+    context(d).call("ki_compact_map", _MAPS[f], _PREDS[pred], _dtype_code(x), _ptr(x), x.numel(),
+                    ctypes.c_void_p(thr.ctypes.data), None, None, ctypes.c_int64(1), _ptr(out), _stream_ptr(stream, d))
+    return out
 
 
 def vote_compact(x, threshold: float, out_vals=None, out_idx=None, count=None, index_base: int = 1,

@@ -43,6 +43,8 @@ SIGNATURES = {
     "ki_vcopy_host": (_i32, [_vp, _vp, _vp, _sz, _vp]),
     "ki_vcopy_2d": (_i32, [_vp, _vp, _sz, _vp, _sz, _sz, _sz, _vp]),
     "ki_scan_rows": (_i32, [_vp, _i32, _i32, _i32, _vp, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
+    "ki_mapreduce": (_i32, [_vp, _i32, _i32, _i32, _vp, _sz, _vp, _vp]),
+    "ki_compact_map": (_i32, [_vp, _i32, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _i64, _vp, _vp]),
     "ki_vcopy_strided": (_i32, [_vp, _vp, _i64, _vp, _i64, _sz, _sz, _vp]),
     "ki_reduce_sum_f32": (_i32, [_vp, _vp, _sz, _vp, _vp, _vp]),
     "ki_reduce_sum_i64": (_i32, [_vp, _vp, _sz, _vp, _vp]),

@@ -287,6 +287,38 @@ def reduce_op(op: str, x: np.ndarray):
     return accumulate(op, x)[-1]
 
 
+def apply_map(f, x: np.ndarray) -> np.ndarray:
+    """abs / abs2 in the element type, as Base computes them (integers wrap: abs(typemin) is typemin,
+    abs2 is x*x modulo 2^bits; abs is the identity on unsigned types)."""
+    x = np.ascontiguousarray(x)
+    if f is None:
+        return x
+    with np.errstate(over="ignore"):
+        if f == "abs":
+            return x if x.dtype.kind == "u" else np.abs(x).astype(x.dtype)
+        if f == "abs2":
+            return (x * x).astype(x.dtype)
+    raise ValueError(f)
+
+
+def mapreduce_op(f, op: str, x: np.ndarray):
+    """mapreduce(f, op, x): the map in the element type, then reduce_op."""
+    return reduce_op(op, apply_map(f, x))
+
+
+_CMP = {">": np.greater, ">=": np.greater_equal, "<": np.less, "<=": np.less_equal, "==": np.equal,
+        "!=": np.not_equal}
+
+
+def filter_pred(x: np.ndarray, pred: str, thr, f=None, index_base: int = 1):
+    """filter(v -> f(v) pred thr, x) and findall (index_base-based Int32 indices): IEEE comparisons in
+    the element type, order preserved, the kept elements x's own."""
+    x = np.ascontiguousarray(x)
+    keep = _CMP[pred](apply_map(f, x), x.dtype.type(thr))
+    idx = np.nonzero(keep)[0]
+    return x[idx], (idx + index_base).astype(np.int32)
+
+
 def filter_gt_f32(x: np.ndarray, thr: float, index_base: int = 1, nthreads: int = 0):
     x = np.ascontiguousarray(x, dtype=np.float32)
     k = int(lib().ko_filter_gt_f32(_ptr(x), x.size, thr, None, None, index_base, nthreads))

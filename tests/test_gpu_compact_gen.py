@@ -163,3 +163,45 @@ def test_compact_generic_vs_oracle(KI, dev, dt, pred):
         assert np.array_equal(idx.cpu().numpy(), (keep + 1).astype(np.int32)), (n, off)
         assert np.array_equal(vals.cpu().numpy().view(np.uint8), x[keep].view(np.uint8)), (n, off)
     KI.context(0).check()
+
+
+@pytest.mark.parametrize("dt", [np.int32, np.uint32, np.int64, np.uint64, np.float32, np.float64],
+                         ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("f", ["abs", "abs2"])
+def test_compact_mapped_vs_oracle(KI, oracle, dev, dt, f):
+    """Fused map-then-compact: filter(v -> f(v) pred t, x) keeps x's own elements; integer maps wrap
+    (abs(typemin), abs2 overflow), as Base's do."""
+    import torch
+
+    rng = np.random.default_rng(29)
+    info = np.iinfo(dt) if np.dtype(dt).kind != "f" else None
+    for n, off in [(1, 0), (1000, 1), (16385, 0), ((1 << 20) + 13, 1)]:
+        if info is None:
+            base = (rng.standard_normal(n + off) * 2).astype(dt)
+            base[rng.integers(0, n + off, 4)] = np.nan
+            base[rng.integers(0, n + off, 4)] = -0.0
+            thr = 1.5
+        else:
+            base = rng.integers(info.min, info.max, n + off, dtype=dt, endpoint=True)
+            base[rng.integers(0, n + off, 4)] = info.min
+            base[: min(64, n + off)] = rng.integers(-20 if info.min < 0 else 0, 20, min(64, n + off)).astype(dt)
+            thr = 50 if f == "abs2" else 7
+        x = base[off:]
+        xd = torch.from_numpy(base).to(dev)[off:]
+        for pred in (">", "<=", "!="):
+            vals, idx, cnt = KI.compact(xd, pred, thr, f=f)
+            want_v, want_i = oracle.filter_pred(x, pred, thr, f=f)
+            assert cnt.item() == want_i.size, (n, off, pred)
+            assert np.array_equal(idx.cpu().numpy(), want_i), (n, off, pred)
+            assert np.array_equal(vals.cpu().numpy().view(np.uint8), want_v.view(np.uint8)), (n, off, pred)
+            assert KI.count(xd, pred, thr, f=f).item() == want_i.size
+    KI.context(0).check()
+
+
+def test_count_plain(KI, oracle, dev):
+    import torch
+
+    x = np.random.default_rng(3).standard_normal((1 << 22) + 5).astype(np.float32)
+    xd = torch.from_numpy(x).to(dev)
+    for pred, t in ((">", 0.5), ("<", -1.0), ("==", 0.0)):
+        assert KI.count(xd, pred, t).item() == oracle.filter_pred(x, pred, t)[1].size

@@ -258,3 +258,24 @@ def test_scan_rows_strided_output_and_in_place(KI, oracle, dev):
     with pytest.raises(KI.KIArgumentError):  # rows overlapping another layout
         KI.scan_rows(xd[:, :4000], "+", out=xd[:, 1000:])
     KI.context(0).check()
+
+
+@pytest.mark.parametrize("dt", NP_TYPES, ids=lambda d: np.dtype(d).name)
+@pytest.mark.parametrize("f", ["abs", "abs2"])
+def test_mapreduce(KI, oracle, dev, dt, f):
+    """mapreduce(f, op, x) for f in abs, abs2 and op in +, max, min: the map in the element type (integer
+    wrap-around included), then Base's reduce."""
+    for k, n in enumerate([1, 33, 4099, (1 << 20) + 7]):
+        x = _data(dt, n, 300 + k, "+")  # finite floats: a float sum of abs / abs2 stays finite
+        xd = _to_dev(x, dev)
+        for op in ("+", "max", "min"):
+            got = KI.mapreduce(f, op, xd).cpu().numpy().reshape(1)
+            want = np.array([oracle.mapreduce_op(f, op, x)])
+            if np.dtype(dt).kind == "f" and op == "+":
+                scale = float(np.abs(oracle.apply_map(f, x).astype(np.float64)).sum())
+                assert abs(float(got[0]) - float(want[0])) <= 1e-5 * math.log2(max(2, n)) * scale, (n, op)
+            else:
+                _check(got, want.astype(got.dtype), x, op)
+    with pytest.raises(KI.KIArgumentError):
+        KI.mapreduce(f, "*", _to_dev(_data(dt, 10, 1), dev))
+    KI.context(0).check()

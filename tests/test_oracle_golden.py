@@ -221,3 +221,18 @@ def test_accumulate_products_bitwise_and_small_integers(oracle):
         oracle.reduce_op("|", np.zeros(0, dtype=np.int32))
     with pytest.raises(ValueError):
         oracle.accumulate("xor", f)
+
+
+def test_maps_follow_base_integer_semantics(oracle):
+    """abs(typemin) == typemin, abs2 wraps in the element type, abs is the identity on unsigned;
+    filter_pred keeps the original elements."""
+    i8 = np.array([-128, -3, 5, 127], dtype=np.int8)
+    assert oracle.apply_map("abs", i8).tolist() == [-128, 3, 5, 127]
+    assert oracle.apply_map("abs2", i8).tolist() == [0, 9, 25, 1]
+    i16 = np.array([300, -200], dtype=np.int16)
+    assert oracle.apply_map("abs2", i16).tolist() == [(90000 + 32768) % 65536 - 32768, (40000 + 32768) % 65536 - 32768]
+    u8 = np.array([200, 3], dtype=np.uint8)
+    assert oracle.apply_map("abs", u8).tolist() == [200, 3]
+    v, i = oracle.filter_pred(np.array([-3.0, 1.0, 2.5, -0.5], dtype=np.float32), ">", 1.5, f="abs")
+    assert v.tolist() == [-3.0, 2.5] and i.tolist() == [1, 3]
+    assert oracle.mapreduce_op("abs2", "+", np.array([3, -4], dtype=np.int32)) == 25

@@ -27,6 +27,12 @@ namespace {
 #ifndef KI_REDUCE_UNROLL
 #define KI_REDUCE_UNROLL 4
 #endif
+#ifndef KI_REDUCE_TAIL_BATCH
+#define KI_REDUCE_TAIL_BATCH 1
+#endif
+#ifndef KI_REDUCE_FOLD_BATCH
+#define KI_REDUCE_FOLD_BATCH 8
+#endif
 #ifndef KI_REDUCE_BLOCKS_PER_SM
 #define KI_REDUCE_BLOCKS_PER_SM 8
 #endif
@@ -92,11 +98,23 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) acc = Tr::op(acc, fold_vec<T, Op, M>(v[u]));
     }
+#if KI_REDUCE_TAIL_BATCH
+    {  // the last (fewer than kUnroll) vectors of this thread, requested together
+        V v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+            if (i + u * stride < nvec) v[u].raw = __ldcs(xv + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+            if (i + u * stride < nvec) acc = Tr::op(acc, fold_vec<T, Op, M>(v[u]));
+    }
+#else
     for (; i < nvec; i += stride) {
         V v;
         v.raw = __ldcs(xv + i);
         acc = Tr::op(acc, fold_vec<T, Op, M>(v));
     }
+#endif
     // unaligned head and the tail that does not fill a vector
     if (blockIdx.x == 0) {
         const size_t tail0 = head + nvec * kVec;
@@ -115,8 +133,23 @@ __global__ void __launch_bounds__(kThreads)
     if (!is_last) return;
     ki::fence<ki::Scope::Device, ki::Order::AcqRel>();
     A r = id;
+#if KI_REDUCE_FOLD_BATCH > 1
+    // all of a thread's partials requested before any is folded (one L2 round trip, not one per
+    // partial); the fold order is the same as one at a time: b = tid, tid + kThreads, ...
+    for (unsigned b0 = 0; b0 < gridDim.x; b0 += KI_REDUCE_FOLD_BATCH * kThreads) {
+        A v[KI_REDUCE_FOLD_BATCH];
+#pragma unroll
+        for (int u = 0; u < KI_REDUCE_FOLD_BATCH; ++u) {
+            const unsigned b = b0 + (unsigned)u * kThreads + threadIdx.x;
+            v[u] = b < gridDim.x ? ki::load<ki::Order::Relaxed, ki::Scope::Device>(partials + b) : id;
+        }
+#pragma unroll
+        for (int u = 0; u < KI_REDUCE_FOLD_BATCH; ++u) r = Tr::op(r, v[u]);
+    }
+#else
     for (unsigned b = threadIdx.x; b < gridDim.x; b += kThreads)
         r = Tr::op(r, ki::load<ki::Order::Relaxed, ki::Scope::Device>(partials + b));
+#endif
     __syncthreads();  // sm reuse
     r = block_fold(r, sm, f, id);
     if (threadIdx.x == 0) {

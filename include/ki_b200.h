@@ -112,8 +112,10 @@ int ki_vcopy_host(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, void* 
 int ki_vcopy_2d(ki_ctx* ctx, void* dst, size_t dpitch, const void* src, size_t spitch, size_t width_bytes,
                 size_t height, void* stream);
 /* ki_vcopy_strided: dst[i*dst_stride] = src[i*src_stride] for i < count, elements of elem_bytes
- * (1, 2, 4, 8 or 16) with strides in elements of either sign (view(x, n:-2:1)); both pointers aligned
- * to the element size; src_stride 0 broadcasts one element; the ranges must not overlap. */
+ * (1 to 65536: plain types and structs of any size, e.g. 12-byte structs, which the reference moves
+ * field by field) with strides in elements of either sign (view(x, n:-2:1)); both pointers aligned
+ * to the largest power of two (at most 16) that divides elem_bytes; src_stride 0 broadcasts one
+ * element; the ranges must not overlap. */
 int ki_vcopy_strided(ki_ctx* ctx, void* dst, int64_t dst_stride, const void* src, int64_t src_stride,
                      size_t elem_bytes, size_t count, void* stream);
 

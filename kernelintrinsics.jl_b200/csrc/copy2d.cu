@@ -12,9 +12,13 @@
 //                     (ki/bytes.cuh), so a row misaligned against its destination still reads
 //                     whole aligned 16-byte words.  Each row has its own alignment when a pitch is
 //                     not a multiple of 16; the word shift is picked per row.
-//   ki_vcopy_strided  count elements of 1, 2, 4, 8 or 16 bytes with element strides of either sign
-//                     (view(x, 1:2:n), a row of a column-major matrix, reverse(view)): one natural
-//                     load and store per element, four in flight per thread.
+//   ki_vcopy_strided  count elements with element strides of either sign (view(x, 1:2:n), a row
+//                     of a column-major matrix, reverse(view)).  Elements of 1, 2, 4, 8 or 16
+//                     bytes: one natural load and store per element, four in flight per thread.
+//                     Any other size (a struct of 3, 12 or 40 bytes, which the reference moves
+//                     field by field through its scalar fallback): each element as words of the
+//                     largest power of two that divides its size (at most 16 bytes), consecutive
+//                     threads on consecutive words of an element.
 #include "ki/bytes.cuh"
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
@@ -134,6 +138,21 @@ __global__ void __launch_bounds__(kThreads) strided_kernel(uint8_t* dst, int64_t
     }
 }
 
+// Elements of nw words of W bytes (element sizes that are not 1, 2, 4, 8 or 16); strides in bytes.
+template <int W>
+__global__ void __launch_bounds__(kThreads) strided_words_kernel(uint8_t* dst, int64_t dstride_b, const uint8_t* src,
+                                                                 int64_t sstride_b, size_t count, unsigned nw) {
+    using Wt = typename Word<W>::type;
+    const size_t total = count * nw;
+    const size_t n_threads = (size_t)gridDim.x * kThreads;
+    for (size_t j = (size_t)blockIdx.x * kThreads + threadIdx.x; j < total; j += n_threads) {
+        const size_t i = j / nw;
+        const size_t q = j - i * nw;
+        const Wt v = __ldcs(reinterpret_cast<const Wt*>(src + (int64_t)i * sstride_b + (int64_t)(q * W)));
+        __stcs(reinterpret_cast<Wt*>(dst + (int64_t)i * dstride_b + (int64_t)(q * W)), v);
+    }
+}
+
 size_t grid_for(ki_ctx* ctx, size_t warps_of_work) {
     size_t blocks = (warps_of_work + (kThreads / 32) - 1) / (kThreads / 32);
     const size_t cap = (size_t)ctx->sm_count * (2048 / kThreads);
@@ -179,11 +198,15 @@ extern "C" int ki_vcopy_strided(ki_ctx* ctx, void* dst, int64_t dst_stride, cons
     KI_CHECK_CTX(ctx);
     if (count == 0) return KI_OK;
     if (!dst || !src) return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: null pointer");
-    if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8 && elem_bytes != 16)
-        return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: element size must be 1, 2, 4, 8 or 16 bytes");
-    if (!ki::aligned(dst, elem_bytes) || !ki::aligned(src, elem_bytes))
-        return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: pointers must be aligned to the element size");
-    const int64_t lim = INT64_MAX / 16 / (int64_t)(count > 0 ? count : 1);
+    if (elem_bytes == 0 || elem_bytes > 65536)
+        return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: element size must be 1 to 65536 bytes");
+    size_t word = 16;  // the largest power of two (<= 16) that divides the element size
+    while (elem_bytes % word) word >>= 1;
+    if (!ki::aligned(dst, word) || !ki::aligned(src, word))
+        return ki::set_error(ctx, KI_ERR_ARG,
+                             "vcopy_strided: pointers must be aligned to the largest power of two (<= 16) dividing the "
+                             "element size");
+    const int64_t lim = INT64_MAX / (int64_t)elem_bytes / (int64_t)(count > 0 ? count : 1);
     if (dst_stride > lim || dst_stride < -lim || src_stride > lim || src_stride < -lim)
         return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: stride too large");
     if (count > 1 && dst_stride == 0) return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: zero destination stride");
@@ -193,9 +216,23 @@ extern "C" int ki_vcopy_strided(ki_ctx* ctx, void* dst, int64_t dst_stride, cons
     if (dl < sh && sl < dh) return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: source and destination ranges overlap");
     KI_GUARD(ctx);
     cudaStream_t s = ki::as_stream(stream);
-    const unsigned g = (unsigned)grid_for(ctx, (count + 32 * kUnroll - 1) / (32 * kUnroll));
     uint8_t* d = static_cast<uint8_t*>(dst);
     const uint8_t* sp = static_cast<const uint8_t*>(src);
+    if (word != elem_bytes) {  // a struct: nw words of `word` bytes per element
+        const unsigned nw = (unsigned)(elem_bytes / word);
+        if (count > SIZE_MAX / nw) return ki::set_error(ctx, KI_ERR_ARG, "vcopy_strided: too many elements");
+        const unsigned g = (unsigned)grid_for(ctx, (count * nw + 31) / 32);
+        const int64_t dsb = dst_stride * (int64_t)elem_bytes, ssb = src_stride * (int64_t)elem_bytes;
+        switch (word) {
+            case 1: strided_words_kernel<1><<<g, kThreads, 0, s>>>(d, dsb, sp, ssb, count, nw); break;
+            case 2: strided_words_kernel<2><<<g, kThreads, 0, s>>>(d, dsb, sp, ssb, count, nw); break;
+            case 4: strided_words_kernel<4><<<g, kThreads, 0, s>>>(d, dsb, sp, ssb, count, nw); break;
+            case 8: strided_words_kernel<8><<<g, kThreads, 0, s>>>(d, dsb, sp, ssb, count, nw); break;
+            default: strided_words_kernel<16><<<g, kThreads, 0, s>>>(d, dsb, sp, ssb, count, nw); break;
+        }
+        return ki::check_launch(ctx, "strided_words_kernel launch");
+    }
+    const unsigned g = (unsigned)grid_for(ctx, (count + 32 * kUnroll - 1) / (32 * kUnroll));
     switch (elem_bytes) {
         case 1: strided_kernel<1><<<g, kThreads, 0, s>>>(d, dst_stride, sp, src_stride, count); break;
         case 2: strided_kernel<2><<<g, kThreads, 0, s>>>(d, dst_stride, sp, src_stride, count); break;

@@ -443,17 +443,23 @@ def vcopy_2d(dst, dpitch: int, src, spitch: int, width: int, height: int, dst_of
 
 
 def vcopy_strided(dst, dst_stride: int, src, src_stride: int, count: int, dst_start: int = 0, src_start: int = 0,
-                  stream=None):
+                  elem_bytes: Optional[int] = None, stream=None):
     """dst[dst_start + i*dst_stride] = src[src_start + i*src_stride] for i < count, in elements of the
-    tensors' (equal) element size; strides of either sign, as Julia's strided and reversed views."""
+    tensors' (equal) element size, or of ``elem_bytes`` bytes (a struct type held in byte tensors);
+    strides of either sign, as Julia's strided and reversed views."""
     d = _dev(dst)
-    es = dst.element_size()
-    if src.element_size() != es:
-        raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_strided: element sizes differ")
+    if elem_bytes is None:
+        es = dst.element_size()
+        if src.element_size() != es:
+            raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_strided: element sizes differ")
+    else:
+        es = int(elem_bytes)
+        if es <= 0:
+            raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_strided: element size must be positive")
     if count > 0:
         for t, st, n0 in ((dst, dst_stride, dst_start), (src, src_stride, src_start)):
             last = n0 + (count - 1) * st
-            if min(n0, last) < 0 or max(n0, last) >= t.numel():
+            if min(n0, last) < 0 or (max(n0, last) + 1) * es > t.numel() * t.element_size():
                 raise KIArgumentError(_abi.KI_ERR_ARG, "vcopy_strided: range outside the tensors")
     context(d).call("ki_vcopy_strided", ctypes.c_void_p(dst.data_ptr() + dst_start * es), int(dst_stride),
                     ctypes.c_void_p(src.data_ptr() + src_start * es), int(src_stride), es, int(count),

@@ -71,6 +71,27 @@ def test_strided_elements(KI, oracle, dev, dtype):
     KI.context(0).check()
 
 
+@pytest.mark.parametrize("elem", [3, 6, 12, 24, 40, 48])
+def test_strided_structs(KI, oracle, dev, elem):
+    """Struct elements of sizes that are not 1, 2, 4, 8 or 16 bytes (the reference's scalar fallback
+    for non-power-of-two types), held in byte buffers, strides of either sign."""
+    import torch
+
+    vt = np.dtype(f"V{elem}")
+    n = 40_000
+    src_h = _bytes(oracle, 26, n * elem)
+    src = torch.from_numpy(src_h.copy()).to(dev)
+    for count, ss, ds, s0, d0 in [(1, 1, 1, 0, 0), (999, 2, 3, 7, 1), (5000, -3, 1, 39_999, 10), (20_000, 1, -2, 0, 39_999),
+                                  (333, 0, 5, 12, 0)]:
+        dst_h = _bytes(oracle, 27, n * elem)
+        dst = torch.from_numpy(dst_h.copy()).to(dev)
+        KI.vcopy_strided(dst, ds, src, ss, count, dst_start=d0, src_start=s0, elem_bytes=elem)
+        want = dst_h.copy().view(vt)
+        oracle.copy_strided(want, ds, src_h.view(vt), ss, count, dst_start=d0, src_start=s0)
+        assert np.array_equal(dst.cpu().numpy(), want.view(np.uint8)), (elem, count, ss, ds)
+    KI.context(0).check()
+
+
 def test_copyto_views(KI, dev):
     """copyto! on torch views: a column-major block (2-D, contiguous rows), a strided 1-D view, a
     contiguous range."""

@@ -31,8 +31,9 @@
 // with the lines demoted to normal priority after the second read: 0.48 ms), evict-first second
 // reads (0.50), tiles kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-
 // element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
-// per SM of 16 warps over 64 KiB tiles (0.48), looking tile k up right after its count, early
-// tickets.  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
+// per SM of 16 warps over 64 KiB tiles (0.47-0.48), 16 rows in flight per warp in the second pass
+// (0.54: spills), two CTAs of 12 warps over 48 KiB tiles (0.51), looking tile k up right after its
+// count, early tickets.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %, warps 41 % active).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #pragma once
 
 #include "ki/common.cuh"
@@ -63,7 +64,10 @@ constexpr int kWorkThreads = 32 * kWorkWarps;
 constexpr int kThreads = kWorkThreads + 32;
 constexpr int kRows = KI_COMPACT_ROWS;  // rows of 32 lanes x one 16-byte vector per work warp
 constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 512;  // 64 KiB: 16384 elements of 4 bytes or 8192 of 8
-constexpr int kBatch = 8;             // rows loaded at once in the second pass
+#ifndef KI_COMPACT_BATCH
+#define KI_COMPACT_BATCH 8
+#endif
+constexpr int kBatch = KI_COMPACT_BATCH;  // rows loaded at once in the second pass
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 

@@ -11,7 +11,8 @@
 //                     aligned 16-byte stores whose source words are re-aligned in registers
 //                     (ki/bytes.cuh), so a row misaligned against its destination still reads
 //                     whole aligned 16-byte words.  Each row has its own alignment when a pitch is
-//                     not a multiple of 16; the word shift is picked per row.
+//                     not a multiple of 16; the word shift is picked per row.  Rows of at most 384
+//                     bytes take one thread per 16-byte chunk instead (a warp then spans several rows).
 //   ki_vcopy_strided  count elements with element strides of either sign (view(x, 1:2:n), a row
 //                     of a column-major matrix, reverse(view)).  Elements of 1, 2, 4, 8 or 16
 //                     bytes: one natural load and store per element, four in flight per thread.
@@ -109,6 +110,67 @@ __global__ void __launch_bounds__(kThreads) vcopy2d_kernel(Copy2DArgs a) {
     }
 }
 
+// Narrow rows (width <= kNarrowRow bytes): one thread per 16-byte destination chunk instead of one
+// warp per row, so a warp covers several rows.  Measured (fraction of the copy peak, narrow against
+// warp-per-row): 64-byte rows 0.24 / 0.08, 256-byte rows 0.29 / 0.22, 512-byte rows 0.35 / 0.41,
+// 1000-byte rows 0.46 / 0.51; hence the 384-byte threshold.  A row owns width/16 + 3 slots: its
+// head bytes, its tail bytes and its body chunks.  A body chunk whose source is misaligned reads the two aligned
+// source words it straddles (both hold bytes of this row) and re-aligns them in registers; head and
+// tail (< 16 bytes each) are copied byte by byte, their loads issued together.
+#ifndef KI_COPY2D_NARROW
+#define KI_COPY2D_NARROW 384
+#endif
+constexpr size_t kNarrowRow = KI_COPY2D_NARROW;
+
+template <int WS>
+__device__ __forceinline__ uint4 realign_pair(const uint4* sa, unsigned sh) {
+    return ki::realign<WS>(sa[0], sa[1], sh);
+}
+
+// I: the slot index type (32-bit whenever the slots fit: a 64-bit division per chunk costs more than
+// the chunk's copy).
+template <class I>
+__global__ void __launch_bounds__(kThreads) vcopy2d_narrow_kernel(Copy2DArgs a) {
+    const I slots = (I)(a.width / 16 + 3);
+    const I total = (I)a.height * slots;
+    const I n_threads = (I)gridDim.x * kThreads;
+    for (I j = (I)blockIdx.x * kThreads + threadIdx.x; j < total; j += n_threads) {
+        const I row = j / slots, q = j - row * slots;
+        uint8_t* dr = a.dst + (size_t)row * a.dpitch;
+        const uint8_t* sr = a.src + (size_t)row * a.spitch;
+        size_t head = (16 - ((uintptr_t)dr & 15)) & 15;
+        if (head > a.width) head = a.width;
+        const size_t nc = (a.width - head) / 16;
+        if (q < 2) {  // q = 0: the head bytes; q = 1: the tail bytes
+            const size_t b0 = q == 0 ? 0 : head + nc * 16;
+            const size_t nb = q == 0 ? head : a.width - head - nc * 16;
+            uint8_t v[15];
+#pragma unroll
+            for (int b = 0; b < 15; ++b)
+                if ((size_t)b < nb) v[b] = sr[b0 + b];
+#pragma unroll
+            for (int b = 0; b < 15; ++b)
+                if ((size_t)b < nb) dr[b0 + b] = v[b];
+            continue;
+        }
+        const size_t k = (size_t)q - 2;
+        if (k >= nc) continue;
+        uint4* d = reinterpret_cast<uint4*>(dr + head) + k;
+        const uintptr_t sb = (uintptr_t)(sr + head) + 16 * k;
+        const unsigned mis = (unsigned)(sb & 15);
+        const uint4* sa = reinterpret_cast<const uint4*>(sb - mis);
+        const unsigned sh = (mis & 3) * 8;
+        uint4 r;
+        switch (mis >> 2) {
+            case 0: r = mis == 0 ? sa[0] : realign_pair<0>(sa, sh); break;
+            case 1: r = realign_pair<1>(sa, sh); break;
+            case 2: r = realign_pair<2>(sa, sh); break;
+            default: r = realign_pair<3>(sa, sh); break;
+        }
+        *d = r;
+    }
+}
+
 template <int B>
 struct Word;
 template <> struct Word<1> { using type = uint8_t; };
@@ -189,6 +251,16 @@ extern "C" int ki_vcopy_2d(ki_ctx* ctx, void* dst, size_t dpitch, const void* sr
     a.width = width;
     a.height = height;
     a.spans = (width / 16 + kSpan) / kSpan;  // at least one: the item that also moves head and tail
+    if (width <= kNarrowRow && height > 1) {
+        const size_t threads = height * (width / 16 + 3);
+        const unsigned g = (unsigned)grid_for(ctx, (threads + 31) / 32);
+        // 32-bit slot indices while every index, and the grid stride past the last one, fits
+        if (threads + (size_t)g * kThreads < (1ull << 32))
+            vcopy2d_narrow_kernel<uint32_t><<<g, kThreads, 0, ki::as_stream(stream)>>>(a);
+        else
+            vcopy2d_narrow_kernel<size_t><<<g, kThreads, 0, ki::as_stream(stream)>>>(a);
+        return ki::check_launch(ctx, "vcopy2d_narrow_kernel launch");
+    }
     vcopy2d_kernel<<<(unsigned)grid_for(ctx, height * a.spans), kThreads, 0, ki::as_stream(stream)>>>(a);
     return ki::check_launch(ctx, "vcopy2d_kernel launch");
 }

@@ -37,7 +37,8 @@ def test_2d_alignments_pitches_and_widths(KI, oracle, dev):
     KI.context(0).check()
 
 
-def test_2d_every_alignment_pair(KI, oracle, dev):
+@pytest.mark.parametrize("width", [200, 600])  # the narrow-row kernel and the warp-per-row kernel
+def test_2d_every_alignment_pair(KI, oracle, dev, width):
     """All 16 x 16 (source, destination) alignments, with a pitch that moves each row's alignment."""
     import torch
 
@@ -46,9 +47,9 @@ def test_2d_every_alignment_pair(KI, oracle, dev):
     dst = torch.zeros(1 << 16, dtype=torch.uint8, device=dev)
     for so, do in itertools.product(range(16), range(16)):
         dst.zero_()
-        KI.vcopy_2d(dst, 600 + 7, src, 600 + 3, 600, 40, dst_offset=do, src_offset=so)
+        KI.vcopy_2d(dst, width + 7, src, width + 3, width, 40, dst_offset=do, src_offset=so)
         want = np.zeros(1 << 16, dtype=np.uint8)
-        oracle.copy_2d(want, 607, src_h, 603, 600, 40, dst_offset=do, src_offset=so)
+        oracle.copy_2d(want, width + 7, src_h, width + 3, width, 40, dst_offset=do, src_offset=so)
         assert np.array_equal(dst.cpu().numpy(), want), (so, do)
 
 

@@ -62,7 +62,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="", help="comma list of kernels to run under 'kernels'")
-    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm", "scan_f32", "rows"],
+    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm", "scan_f32", "scan_u8", "rows"],
                    help="run only this kernel, --profile-launches times, on a small case (for ncu)")
     p.add_argument("--profile-n", type=int, default=0, help="elements (bytes for copy; M=N=K for gemm)")
     p.add_argument("--profile-launches", type=int, default=3)
@@ -116,6 +116,13 @@ def run_profile(args):
         y = torch.empty_like(x)
         fn = lambda: KI.scan(x, "+", out=y)
         alg = 8 * n
+    elif k == "scan_u8":
+        n = n or (1 << 26)  # UInt8 cumsum into UInt64
+        x = torch.empty(n, dtype=torch.uint8, device=dev)
+        KI.fill_bytes(x, seed=2)
+        y = torch.empty(n, dtype=torch.uint64, device=dev)
+        fn = lambda: KI.scan(x, "+", out=y)
+        alg = 9 * n
     elif k == "rows":
         n = n or 8192  # n x n Float32, one sum per row
         x = torch.empty((n, n), dtype=torch.float32, device=dev)

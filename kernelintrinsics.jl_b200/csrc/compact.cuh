@@ -33,7 +33,11 @@
 // element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
 // per SM of 16 warps over 64 KiB tiles (0.47-0.48), 16 rows in flight per warp in the second pass
 // (0.54: spills), two CTAs of 12 warps over 48 KiB tiles (0.51), looking tile k up right after its
-// count, early tickets.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %, warps 41 % active).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
+// count, early tickets, and compacting each tile into shared memory right after its count so that
+// its write-out reads no global memory (32 KiB tiles double-buffered, a tile-sized compacted buffer
+// with 16-bit indices, 2 CTAs per SM: 0.645 ms; the extra pass and the smaller tiles in flight cost
+// more than the re-reads).  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %, warps 41 %
+// active).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #pragma once
 
 #include "ki/common.cuh"

@@ -42,15 +42,21 @@ constexpr int kWorkWarps = 31;
 constexpr int kLookWarp = kWorkWarps;
 constexpr int kWorkThreads = 32 * kWorkWarps;
 constexpr int kThreads = kWorkThreads + 32;
-constexpr int kRowsPerWarp = 8;
-constexpr size_t kTileBytes = (size_t)kWorkWarps * kRowsPerWarp * 32 * 16;  // 126976 B
+#ifndef KI_SCAN_ANY_ROWS_2B
+#define KI_SCAN_ANY_ROWS_2B 8
+#endif
+#ifndef KI_SCAN_ANY_ROWS_1B
+#define KI_SCAN_ANY_ROWS_1B 8
+#endif
 
 template <class T>
 struct Shape {
     static constexpr int kE = (int)(16 / sizeof(T));        // elements per lane per row
     static constexpr int kRow = 32 * kE;                     // elements per row
-    static constexpr int kSpan = kRowsPerWarp * kRow;         // elements per warp
+    static constexpr int kRows = sizeof(T) >= 4 ? 8 : sizeof(T) == 2 ? KI_SCAN_ANY_ROWS_2B : KI_SCAN_ANY_ROWS_1B;
+    static constexpr int kSpan = kRows * kRow;               // elements per warp
     static constexpr int kTile = kWorkWarps * kSpan;          // elements per tile
+    static constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 32 * 16;  // 126976 B at 8 rows
 };
 
 // The input is rows x cols (rows = 1 for a plain scan): row r starts ld_in elements after row r-1
@@ -127,8 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
         ticket = t;
         if (bulk_ok(t)) {
             ki::fence_proxy_async_smem();
-            ki::mbar_arrive_expect_tx(&bar, (uint32_t)kTileBytes);
-            ki::bulk_g2s_keep(sb, in + where(t).in_off, (uint32_t)kTileBytes, &bar);
+            ki::mbar_arrive_expect_tx(&bar, (uint32_t)S::kTileBytes);
+            ki::bulk_g2s_keep(sb, in + where(t).in_off, (uint32_t)S::kTileBytes, &bar);
         }
     };
     if (tid == 0) {
@@ -169,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             }
             A s = id;
 #pragma unroll
-            for (int j = 0; j < kRowsPerWarp; ++j) {
+            for (int j = 0; j < S::kRows; ++j) {
                 ki::Packed16<T> v;
                 v.raw = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
 #pragma unroll
@@ -207,9 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             const T pad = ki::pad_value<T, Op>();
             // rows in flight: all 8 for 4- and 8-byte elements; 1- and 2-byte elements take more
             // registers per row on the way out, so they go KI_SCAN_ANY_SMALL_BATCH rows at a time
-            constexpr int kB = sizeof(T) >= 4 ? kRowsPerWarp : KI_SCAN_ANY_SMALL_BATCH;
+            constexpr int kB = sizeof(T) >= 4 ? S::kRows : (KI_SCAN_ANY_SMALL_BATCH < S::kRows ? KI_SCAN_ANY_SMALL_BATCH : S::kRows);
+            static_assert(S::kRows % kB == 0, "row batches");
 #pragma unroll 1
-            for (int j0 = 0; j0 < kRowsPerWarp; j0 += kB) {
+            for (int j0 = 0; j0 < S::kRows; j0 += kB) {
             ki::Packed16<T> v[kB];
 #pragma unroll
             for (int jj = 0; jj < kB; ++jj) {
@@ -456,12 +463,12 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, const Sca
     if (grid > ntiles) grid = ntiles;
     if (excl) {
         KI_CUDA(ctx, cudaFuncSetAttribute(scan_any_kernel<T, Op, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)kTileBytes));
-        scan_any_kernel<T, Op, true><<<(unsigned)grid, kThreads, kTileBytes, s>>>(a);
+                                          (int)S::kTileBytes));
+        scan_any_kernel<T, Op, true><<<(unsigned)grid, kThreads, S::kTileBytes, s>>>(a);
     } else {
         KI_CUDA(ctx, cudaFuncSetAttribute(scan_any_kernel<T, Op, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)kTileBytes));
-        scan_any_kernel<T, Op, false><<<(unsigned)grid, kThreads, kTileBytes, s>>>(a);
+                                          (int)S::kTileBytes));
+        scan_any_kernel<T, Op, false><<<(unsigned)grid, kThreads, S::kTileBytes, s>>>(a);
     }
     return ki::check_launch(ctx, "scan_any_kernel launch");
 }

@@ -12,7 +12,8 @@
 //                     (ki/bytes.cuh), so a row misaligned against its destination still reads
 //                     whole aligned 16-byte words.  Each row has its own alignment when a pitch is
 //                     not a multiple of 16; the word shift is picked per row.  Rows of at most 384
-//                     bytes take one thread per 16-byte chunk instead (a warp then spans several rows).
+//                     bytes take one thread per 16-byte chunk instead (a warp then spans several
+//                     rows).
 //   ki_vcopy_strided  count elements with element strides of either sign (view(x, 1:2:n), a row
 //                     of a column-major matrix, reverse(view)).  Elements of 1, 2, 4, 8 or 16
 //                     bytes: one natural load and store per element, four in flight per thread.
@@ -114,9 +115,9 @@ __global__ void __launch_bounds__(kThreads) vcopy2d_kernel(Copy2DArgs a) {
 // warp per row, so a warp covers several rows.  Measured (fraction of the copy peak, narrow against
 // warp-per-row): 64-byte rows 0.24 / 0.08, 256-byte rows 0.29 / 0.22, 512-byte rows 0.35 / 0.41,
 // 1000-byte rows 0.46 / 0.51; hence the 384-byte threshold.  A row owns width/16 + 3 slots: its
-// head bytes, its tail bytes and its body chunks.  A body chunk whose source is misaligned reads the two aligned
-// source words it straddles (both hold bytes of this row) and re-aligns them in registers; head and
-// tail (< 16 bytes each) are copied byte by byte, their loads issued together.
+// head bytes, its tail bytes and its body chunks.  A body chunk whose source is misaligned reads
+// the two aligned source words it straddles (both hold bytes of this row) and re-aligns them in
+// registers; head and tail (< 16 bytes each) are copied byte by byte, their loads issued together.
 #ifndef KI_COPY2D_NARROW
 #define KI_COPY2D_NARROW 384
 #endif

@@ -62,7 +62,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="", help="comma list of kernels to run under 'kernels'")
-    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm", "scan_f32", "scan_u8", "rows"],
+    p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm", "scan_f32", "scan_u8", "rows", "copy2d",
+                            "count"],
                    help="run only this kernel, --profile-launches times, on a small case (for ncu)")
     p.add_argument("--profile-n", type=int, default=0, help="elements (bytes for copy; M=N=K for gemm)")
     p.add_argument("--profile-launches", type=int, default=3)
@@ -123,6 +124,20 @@ def run_profile(args):
         y = torch.empty(n, dtype=torch.uint64, device=dev)
         fn = lambda: KI.scan(x, "+", out=y)
         alg = 9 * n
+    elif k == "copy2d":
+        n = n or 8192  # rows of 32 KiB between pitches 33000 and 40000, odd offsets
+        src = torch.empty(n * 33000 + 16, dtype=torch.uint8, device=dev)
+        KI.fill_bytes(src, seed=2)
+        dst = torch.empty(n * 40000 + 16, dtype=torch.uint8, device=dev)
+        fn = lambda: KI.vcopy_2d(dst, 40000, src, 33000, 32768, n, dst_offset=3, src_offset=11)
+        alg = 2 * 32768 * n
+    elif k == "count":
+        n = n or (1 << 26)  # count(>(0.5), x) over N(0,1) Float32
+        x = torch.empty(n, dtype=torch.float32, device=dev)
+        KI.fill_normal(x, seed=4)
+        c = torch.zeros((), dtype=torch.uint64, device=dev)
+        fn = lambda: KI.count(x, ">", 0.5, out=c)
+        alg = 4 * n
     elif k == "rows":
         n = n or 8192  # n x n Float32, one sum per row
         x = torch.empty((n, n), dtype=torch.float32, device=dev)

@@ -112,12 +112,15 @@ __global__ void __launch_bounds__(kThreads) vcopy2d_kernel(Copy2DArgs a) {
 }
 
 // Narrow rows (width <= kNarrowRow bytes): one thread per 16-byte destination chunk instead of one
-// warp per row, so a warp covers several rows.  Measured (fraction of the copy peak, narrow against
-// warp-per-row): 64-byte rows 0.24 / 0.08, 256-byte rows 0.29 / 0.22, 512-byte rows 0.35 / 0.41,
-// 1000-byte rows 0.46 / 0.51; hence the 384-byte threshold.  A row owns width/16 + 3 slots: its
-// head bytes, its tail bytes and its body chunks.  A body chunk whose source is misaligned reads
-// the two aligned source words it straddles (both hold bytes of this row) and re-aligns them in
-// registers; head and tail (< 16 bytes each) are copied byte by byte, their loads issued together.
+// warp per row, so a warp covers several rows.  A row owns width/16 + 2 slots: its head bytes, its
+// tail bytes and its body chunks.  A body chunk whose source is misaligned reads the two aligned
+// source words it straddles (both hold bytes of this row) and re-aligns them in registers; head and
+// tail (< 16 bytes each) are copied byte by byte, their loads issued together.  Each thread has
+// KI_COPY2D_NARROW_INFLIGHT slots' loads in flight before it stores.  Measured (fraction of the
+// copy peak): 64-byte rows 0.34 (one slot at a time 0.24, warp per row 0.08), 100-byte rows 0.28
+// (0.24), 256-byte rows 0.36 (0.29, warp per row 0.22), 384-byte rows 0.39 (0.31); 512-byte rows
+// run 0.41 warp per row, hence the 384-byte threshold.  Four slots in flight: 0.15-0.29; head and
+// tail in a pass of their own after the bodies: faster on aligned rows, slower on short odd ones.
 #ifndef KI_COPY2D_NARROW
 #define KI_COPY2D_NARROW 384
 #endif
@@ -130,45 +133,76 @@ __device__ __forceinline__ uint4 realign_pair(const uint4* sa, unsigned sh) {
 
 // I: the slot index type (32-bit whenever the slots fit: a 64-bit division per chunk costs more than
 // the chunk's copy).
+#ifndef KI_COPY2D_NARROW_INFLIGHT
+#define KI_COPY2D_NARROW_INFLIGHT 2
+#endif
+
+// One row's layout: head bytes before the 16-byte aligned body, nc body chunks.
+__device__ __forceinline__ void narrow_row(const Copy2DArgs& a, size_t row, uint8_t*& dr, const uint8_t*& sr,
+                                           size_t& head, size_t& nc) {
+    dr = a.dst + row * a.dpitch;
+    sr = a.src + row * a.spitch;
+    head = (16 - ((uintptr_t)dr & 15)) & 15;
+    if (head > a.width) head = a.width;
+    nc = (a.width - head) / 16;
+}
+
 template <class I>
 __global__ void __launch_bounds__(kThreads) vcopy2d_narrow_kernel(Copy2DArgs a) {
-    const I slots = (I)(a.width / 16 + 3);
-    const I total = (I)a.height * slots;
+    constexpr int kIn = KI_COPY2D_NARROW_INFLIGHT;  // slots in flight per thread
     const I n_threads = (I)gridDim.x * kThreads;
-    for (I j = (I)blockIdx.x * kThreads + threadIdx.x; j < total; j += n_threads) {
-        const I row = j / slots, q = j - row * slots;
-        uint8_t* dr = a.dst + (size_t)row * a.dpitch;
-        const uint8_t* sr = a.src + (size_t)row * a.spitch;
-        size_t head = (16 - ((uintptr_t)dr & 15)) & 15;
-        if (head > a.width) head = a.width;
-        const size_t nc = (a.width - head) / 16;
-        if (q < 2) {  // q = 0: the head bytes; q = 1: the tail bytes
-            const size_t b0 = q == 0 ? 0 : head + nc * 16;
-            const size_t nb = q == 0 ? head : a.width - head - nc * 16;
-            uint8_t v[15];
+    const I slots = (I)(a.width / 16 + 2);  // per row: head bytes, tail bytes, then the body chunks
+    const I total = (I)a.height * slots;
+    for (I j0 = (I)blockIdx.x * kThreads + threadIdx.x; j0 < total; j0 += n_threads * kIn) {
+        uint4 r[kIn];
+        uint8_t hv[kIn][15];
+        uint8_t* dp[kIn];
+        int nb[kIn];  // -1: nothing; 16: a body chunk; 0..15: head or tail bytes
 #pragma unroll
-            for (int b = 0; b < 15; ++b)
-                if ((size_t)b < nb) v[b] = sr[b0 + b];
+        for (int u = 0; u < kIn; ++u) {
+            nb[u] = -1;
+            const I j = j0 + (I)u * n_threads;
+            if (j >= total) continue;
+            const I row = j / slots, q = j - row * slots;
+            uint8_t* dr;
+            const uint8_t* sr;
+            size_t head, nc;
+            narrow_row(a, (size_t)row, dr, sr, head, nc);
+            if (q < 2) {
+                const size_t b0 = q == 0 ? 0 : head + nc * 16;
+                const int n = (int)(q == 0 ? head : a.width - head - nc * 16);
 #pragma unroll
-            for (int b = 0; b < 15; ++b)
-                if ((size_t)b < nb) dr[b0 + b] = v[b];
-            continue;
+                for (int b = 0; b < 15; ++b)
+                    if (b < n) hv[u][b] = sr[b0 + b];
+                dp[u] = dr + b0;
+                nb[u] = n;
+                continue;
+            }
+            const size_t k = (size_t)q - 2;
+            if (k >= nc) continue;
+            const uintptr_t sb = (uintptr_t)(sr + head) + 16 * k;
+            const unsigned mis = (unsigned)(sb & 15);
+            const uint4* sa = reinterpret_cast<const uint4*>(sb - mis);
+            const unsigned sh = (mis & 3) * 8;
+            switch (mis >> 2) {
+                case 0: r[u] = mis == 0 ? sa[0] : realign_pair<0>(sa, sh); break;
+                case 1: r[u] = realign_pair<1>(sa, sh); break;
+                case 2: r[u] = realign_pair<2>(sa, sh); break;
+                default: r[u] = realign_pair<3>(sa, sh); break;
+            }
+            dp[u] = dr + head + 16 * k;
+            nb[u] = 16;
         }
-        const size_t k = (size_t)q - 2;
-        if (k >= nc) continue;
-        uint4* d = reinterpret_cast<uint4*>(dr + head) + k;
-        const uintptr_t sb = (uintptr_t)(sr + head) + 16 * k;
-        const unsigned mis = (unsigned)(sb & 15);
-        const uint4* sa = reinterpret_cast<const uint4*>(sb - mis);
-        const unsigned sh = (mis & 3) * 8;
-        uint4 r;
-        switch (mis >> 2) {
-            case 0: r = mis == 0 ? sa[0] : realign_pair<0>(sa, sh); break;
-            case 1: r = realign_pair<1>(sa, sh); break;
-            case 2: r = realign_pair<2>(sa, sh); break;
-            default: r = realign_pair<3>(sa, sh); break;
+#pragma unroll
+        for (int u = 0; u < kIn; ++u) {
+            if (nb[u] == 16) {
+                *reinterpret_cast<uint4*>(dp[u]) = r[u];
+            } else {
+#pragma unroll
+                for (int b = 0; b < 15; ++b)
+                    if (b < nb[u]) dp[u][b] = hv[u][b];
+            }
         }
-        *d = r;
     }
 }
 
@@ -253,10 +287,10 @@ extern "C" int ki_vcopy_2d(ki_ctx* ctx, void* dst, size_t dpitch, const void* sr
     a.height = height;
     a.spans = (width / 16 + kSpan) / kSpan;  // at least one: the item that also moves head and tail
     if (width <= kNarrowRow && height > 1) {
-        const size_t threads = height * (width / 16 + 3);
+        const size_t threads = height * (width / 16 + 2);  // head and tail slots plus the body chunks
         const unsigned g = (unsigned)grid_for(ctx, (threads + 31) / 32);
         // 32-bit slot indices while every index, and the grid stride past the last one, fits
-        if (threads + (size_t)g * kThreads < (1ull << 32))
+        if (threads + (size_t)g * kThreads * KI_COPY2D_NARROW_INFLIGHT < (1ull << 32))
             vcopy2d_narrow_kernel<uint32_t><<<g, kThreads, 0, ki::as_stream(stream)>>>(a);
         else
             vcopy2d_narrow_kernel<size_t><<<g, kThreads, 0, ki::as_stream(stream)>>>(a);

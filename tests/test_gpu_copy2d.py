@@ -37,7 +37,7 @@ def test_2d_alignments_pitches_and_widths(KI, oracle, dev):
     KI.context(0).check()
 
 
-@pytest.mark.parametrize("width", [200, 600])  # the narrow-row kernel and the warp-per-row kernel
+@pytest.mark.parametrize("width", [200, 600, 1500])  # narrow-row kernel (odd pitches up to 1 KiB), warp per row
 def test_2d_every_alignment_pair(KI, oracle, dev, width):
     """All 16 x 16 (source, destination) alignments, with a pitch that moves each row's alignment."""
     import torch

@@ -167,10 +167,15 @@ __device__ __forceinline__ A from_bits(uint64_t b) {
     return v;
 }
 
-// Packing of a value into a status word (state in bits 0-1, wide bit 2).
-template <class A>
+// Packing of a value into a status word (state in bits 0-1, wide bit 2).  LOSSY (a Float64 that is
+// rounded to Float32 at the end anyway): the double rides in the word with its 3 lowest mantissa
+// bits dropped, a relative change below 2^-49.
+template <bool LOSSY = false, class A>
 __device__ __forceinline__ bool pack_value(A v, uint64_t& word_bits) {
-    if constexpr (sizeof(A) == 4) {
+    if constexpr (LOSSY && std::is_same<A, double>::value) {
+        word_bits = to_bits(v) & ~(uint64_t)7;
+        return true;
+    } else if constexpr (sizeof(A) == 4) {
         word_bits = to_bits(v) << 32;
         return true;
     } else if constexpr (std::is_integral<A>::value) {
@@ -182,16 +187,17 @@ __device__ __forceinline__ bool pack_value(A v, uint64_t& word_bits) {
         return false;
     }
 }
-template <class A>
+template <class A, bool LOSSY = false>
 __device__ __forceinline__ A unpack_value(uint64_t w) {
-    if constexpr (sizeof(A) == 4) return from_bits<A>(w >> 32);
+    if constexpr (LOSSY && std::is_same<A, double>::value) return from_bits<A>(w & ~(uint64_t)7);
+    else if constexpr (sizeof(A) == 4) return from_bits<A>(w >> 32);
     else return from_bits<A>((uint64_t)((int64_t)w >> 3));
 }
 
-template <class A>
+template <bool LOSSY = false, class A>
 __device__ __forceinline__ void publish_any(TileStatus st, uint64_t t, uint64_t state, A v) {
     uint64_t packed;
-    if (pack_value(v, packed)) {
+    if (pack_value<LOSSY>(v, packed)) {
         store<Order::Release, Scope::Device>(&st.words[t], packed | state);
     } else {
         uint64_t* side = reinterpret_cast<uint64_t*>(state == kFlagPrefix ? st.incls : st.aggs);
@@ -202,20 +208,20 @@ __device__ __forceinline__ void publish_any(TileStatus st, uint64_t t, uint64_t 
 
 // head: tile t starts a segment (tile 0, or the first tile of a row in a segmented scan); its
 // inclusive prefix is op(init, agg) at once, and no lookback passes it.
-template <class A, class F>
+template <bool LOSSY = false, class A, class F>
 __device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op, bool head) {
-    if (head) publish_any(st, t, kFlagPrefix, op(init, agg));
-    else publish_any(st, t, kFlagAgg, agg);
+    if (head) publish_any<LOSSY>(st, t, kFlagPrefix, op(init, agg));
+    else publish_any<LOSSY>(st, t, kFlagAgg, agg);
 }
-template <class A, class F>
+template <bool LOSSY = false, class A, class F>
 __device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op) {
-    publish_aggregate_any(st, t, agg, init, op, t == 0);
+    publish_aggregate_any<LOSSY>(st, t, agg, init, op, t == 0);
 }
 
 // Run by all 32 lanes of one warp after publish_aggregate_any(t).  Returns the exclusive prefix of
 // tile t (init for a head tile) and publishes tile t's inclusive prefix.  The walk stops at the
 // nearest inclusive prefix, so it never crosses a head tile into an earlier segment.
-template <int K, class A, class F>
+template <int K, bool LOSSY = false, class A, class F>
 __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
                                                     uint32_t* status, uint64_t timeout_ns, bool head) {
     const unsigned lane = lane0();
@@ -269,7 +275,7 @@ __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A
             const int p = (int)lane * K + k;
             if (p <= pos_p && p < 32 * K && end - p >= 0) {
                 if (w[k] & kFlagWide) any_wide = true;
-                else v = op(v, unpack_value<A>(w[k]));
+                else v = op(v, unpack_value<A, LOSSY>(w[k]));
             }
         }
         if (__any_sync(0xffffffffu, any_wide)) {
@@ -289,13 +295,13 @@ __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A
         if (pos_p < 32 * K) break;
         end -= 32 * K;
     }
-    if (lane == 0) publish_any(st, t, kFlagPrefix, op(excl, agg));
+    if (lane == 0) publish_any<LOSSY>(st, t, kFlagPrefix, op(excl, agg));
     return excl;
 }
-template <int K, class A, class F>
+template <int K, bool LOSSY = false, class A, class F>
 __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
                                                     uint32_t* status, uint64_t timeout_ns) {
-    return decoupled_lookback_any<K>(st, t, agg, init, identity, op, status, timeout_ns, t == 0);
+    return decoupled_lookback_any<K, LOSSY>(st, t, agg, init, identity, op, status, timeout_ns, t == 0);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -46,6 +46,9 @@ constexpr int kThreads = kWorkThreads + 32;
 // the copy peak, UInt8 cumsum / Int8 accumulate(max) / UInt8 accumulate(|)): 2 rows 0.41 / 0.25 /
 // 0.35, 4 rows 0.42 / 0.31 / 0.46, 8 rows 0.41 / 0.34 / 0.52, 12 rows 0.39 / 0.33 / 0.48, 14 rows
 // 0.38 / 0.34 / 0.50: the tile size is not what holds these back.
+#ifndef KI_SCAN_ANY_PACK_F32
+#define KI_SCAN_ANY_PACK_F32 1
+#endif
 #ifndef KI_SCAN_ANY_ROWS_2B
 #define KI_SCAN_ANY_ROWS_2B 8
 #endif
@@ -96,6 +99,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
     using R = typename Tr::R;
     using S = Shape<T>;
     constexpr int kE = S::kE;
+    // Float32 sums and products accumulate in Float64 and are rounded to Float32 on output: their
+    // tile values ride in the status words with 3 mantissa bits dropped (no side-array round trips)
+    constexpr bool kLossy = KI_SCAN_ANY_PACK_F32 && std::is_same<T, float>::value && std::is_same<A, double>::value;
     const ki::OpFn<T, Op> op;
     const A id = Tr::identity();
     const A init = ki::from_bits<A>(a.init_bits);
@@ -160,8 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
         if (w == kLookWarp) {
             if (have_old) {
                 PendingAny<A>& o = slot[cur ^ 1];
-                const A ex = ki::decoupled_lookback_any<1>(a.st, o.t, o.agg, init, id, op, a.status, a.timeout_ns,
-                                                           where(o.t).head);
+                const A ex = ki::decoupled_lookback_any<1, kLossy>(a.st, o.t, o.agg, init, id, op, a.status,
+                                                                   a.timeout_ns, where(o.t).head);
                 if (lane == 0) o.tile_excl = ex;
             }
         } else if (new_valid) {
@@ -199,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 if (lane == 0) {
                     e.t = t_new;
                     e.agg = agg;
-                    ki::publish_aggregate_any(a.st, t_new, agg, init, op, p.head);
+                    ki::publish_aggregate_any<kLossy>(a.st, t_new, agg, init, op, p.head);
                 }
             }
         }

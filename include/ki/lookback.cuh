@@ -18,8 +18,8 @@
 #include <cstdint>
 #include <cstring>
 
-#include "common.cuh"
 #include "intrinsics.cuh"
+#include "status.h"
 
 // Sleep between re-reads of a window that still has unpublished tiles (doubles up to the max).
 #ifndef KI_LOOKBACK_MIN_SLEEP_NS

@@ -40,7 +40,8 @@ typedef enum ki_status {
     KI_ERR_CUDA = 2,        /* a CUDA runtime call failed; see ki_last_error_string */
     KI_ERR_TIMEOUT = 3,     /* a bounded device-side wait ran out (lookback flag, mbarrier) */
     KI_ERR_UNSUPPORTED = 4, /* device is not sm_100 / feature not available */
-    KI_ERR_NOMEM = 5        /* scratch allocation failed */
+    KI_ERR_NOMEM = 5,       /* scratch allocation failed */
+    KI_ERR_NCCL = 6         /* an NCCL call of a communicator failed; see ki_last_error_string */
 } ki_status;
 
 /* Scopes and orderings: src/scopes_orderings.jl:13-120 (Workgroup/Device/System;
@@ -82,6 +83,8 @@ int ki_device_info(int device, int* sm_count, int* warp_size, int* cc_major, int
 
 int ki_ctx_create(int device, ki_ctx** out);
 int ki_ctx_destroy(ki_ctx* ctx);
+/* Message of the context's last error; with ctx = NULL, of the calling thread's last failed call that
+ * had no context to hold it (a communicator whose set-up failed). */
 const char* ki_last_error_string(const ki_ctx* ctx);
 /* Synchronises `stream`, returns KI_ERR_TIMEOUT if any device-side wait of this context ran out
  * since the last check (and clears the latch), KI_ERR_CUDA on an asynchronous CUDA error. */
@@ -160,6 +163,19 @@ int ki_reduce_rows(ki_ctx* ctx, int op, int dtype, const void* d_x, size_t rows,
  * bounded by the context's timeout. */
 int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
                           void* stream);
+/* The same scan with its seed read from device memory (*d_seed, one Int64) when the kernel starts, so
+ * a seed computed on the device (a sum of other shards' totals, the last value of a previous chunk)
+ * needs no round trip through the host. */
+int ki_scan_inclusive_i64_dseed(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, const int64_t* d_seed,
+                                void* stream);
+/* cumsum of HOST buffers through the device (Base.cumsum of an Array): 16 MiB chunks cross to the
+ * device, are scanned there (each chunk seeded on the device with the previous chunk's last value)
+ * and come back, both copy directions and the scans overlapped over staging slots owned by the
+ * context (the pipeline of ki_vcopy_host; the two are not re-entrant on one context).  Asynchronous
+ * with respect to the host when both buffers are page-locked; complete when `stream` is.  h_in ==
+ * h_out is allowed; other overlaps return KI_ERR_ARG. */
+int ki_scan_inclusive_i64_host(ki_ctx* ctx, const int64_t* h_in, int64_t* h_out, size_t n, int64_t seed,
+                               void* stream);
 /* Device-wide scan for any of those operators and types (@warpreduce takes any op,
  * src/warp.jl:226-237; the device-wide result is Base.cumsum / accumulate(op, x; init)).
  * op, dtype and the result type as for ki_reduce; d_out holds n values of the result type.
@@ -214,6 +230,71 @@ int ki_compact(ki_ctx* ctx, int pred, int dtype, const void* d_x, size_t n, cons
  * type.  Null d_out_vals and d_out_idx give count(v -> map(v) pred t, x) in d_count. */
 int ki_compact_map(ki_ctx* ctx, int map, int pred, int dtype, const void* d_x, size_t n, const void* h_thr,
                    void* d_out_vals, int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, void* stream);
+
+/* ---- (e) several GPUs: communicators and range-sharded operations ---------------------------
+ * Replaces: device enumeration and selection (src/device.jl:1-19, ext/CUDA/device.jl:4-13) and the
+ * System scope of @access / @fence (ext/CUDA/scopes_ordering.jl:13), from which the reference's users
+ * build multi-GPU code.  A communicator ties one rank to one GPU.  Rank r owns a contiguous shard of
+ * the global array (ki_comm_shard_range gives the default split); the sharded operations below are
+ * collective: every rank calls the same operations in the same order, each on its own shard, and
+ * the calls of one communicator are ordered on one stream.  Only one 8-byte value per rank crosses
+ * between the GPUs per operation, pushed into every peer's exchange buffer with plain peer stores
+ * (st.release.sys) and awaited with bounded ld.acquire.sys loads by a one-warp exchange kernel on
+ * the caller's stream; no host round trip.  A wait that runs out latches KI_ERR_TIMEOUT in the communicator's
+ * context (ki_comm_get_ctx + ki_ctx_check); the communicator is then unusable: ki_comm_abort it.
+ * Ranks must be on distinct GPUs (two ranks on one GPU would wait on one another). */
+typedef struct ki_comm ki_comm;
+#define KI_COMM_MAX_RANKS 64
+typedef struct { char internal[128]; } ki_comm_id;  /* an ncclUniqueId */
+typedef enum { KI_XCHG_AUTO = 0, KI_XCHG_PEER = 1, KI_XCHG_NCCL = 2 } ki_exchange;
+/* Contiguous shard [*lo, *lo + *count) of rank `rank` of n elements: the first n % nranks ranks hold
+ * one element more.  Host only. */
+int ki_comm_shard_range(size_t n, int nranks, int rank, size_t* lo, size_t* count);
+/* One process (or host thread) per GPU: one rank calls ki_comm_get_id and hands the id to the others
+ * (any host channel), then every rank calls ki_comm_init_rank with its own device (0-based) and rank.
+ * NCCL (libnccl.so.2, loaded at run time) exchanges the ranks' buffer handles once; with
+ * KI_XCHG_AUTO or KI_XCHG_PEER the operations then run on peer memory without NCCL, with
+ * KI_XCHG_NCCL (or KI_XCHG_AUTO when peer mappings fail) each exchange is an ncclAllGather of the
+ * 8-byte values on the caller's stream.  Set-up and tear-down waits are bounded on the host (120 s);
+ * on timeout the NCCL communicator is aborted and KI_ERR_TIMEOUT returned.  KI_ERR_UNSUPPORTED: no
+ * NCCL library, or two ranks on one GPU. */
+int ki_comm_get_id(ki_comm_id* id);
+int ki_comm_init_rank(int device, int nranks, int rank, const ki_comm_id* id, int exchange, ki_comm** out);
+/* One host thread driving ndev GPUs (devs: distinct 0-based devices, all peer-capable, else
+ * KI_ERR_UNSUPPORTED): comms[i] is rank i on devs[i].  No NCCL.  Issue the operation for every rank
+ * (each call only enqueues work) before waiting on any of them. */
+int ki_comm_create(int ndev, const int* devs, ki_comm** comms);
+/* Collective for communicators from ki_comm_init_rank (a bounded barrier, then unmap and free);
+ * for ki_comm_create's, destroy every rank's communicator once all their work is complete. */
+int ki_comm_destroy(ki_comm* comm);
+/* Local tear-down without the barrier, for a communicator whose peers failed or left. */
+int ki_comm_abort(ki_comm* comm);
+int ki_comm_info(const ki_comm* comm, int* nranks, int* rank, int* device, int* exchange);
+/* The communicator's own context: ki_ctx_check / ki_ctx_set_wait_timeout_ns on it. */
+int ki_comm_get_ctx(ki_comm* comm, ki_ctx** ctx);
+/* sum of all ranks' Float32 shards: each rank's Float64 partial (ki_reduce_sum_f32) is exchanged and
+ * the partials are added in rank order, so every rank gets the same bits. */
+int ki_reduce_sum_f32_sharded(ki_comm* comm, const float* d_x, size_t n_local, float* d_out_f32, double* d_out_f64,
+                              void* stream);
+/* cumsum of the concatenated Int64 shards: rank r writes its slice.  Phase 1 sums the shard
+ * (ki_reduce_sum_i64), the totals are exchanged, phase 2 is ki_scan_inclusive_i64_dseed seeded on
+ * the device with the sum of the lower ranks' totals. */
+int ki_scan_inclusive_i64_sharded(ki_comm* comm, const int64_t* d_in, int64_t* d_out, size_t n_local, void* stream);
+/* ki_scan_inclusive_i64_sharded with this rank's shard in HOST memory (h_in, h_out, 8-byte aligned;
+ * page-locked for asynchrony): phase 1 brings the shard to the device in 16 MiB chunks and sums each
+ * as it lands, the totals are exchanged, phase 2 scans the chunks in place (seeded on the device)
+ * and sends each back as soon as it is done.  The device copy of the shard lives in the
+ * communicator's scratch.  With one rank it is ki_scan_inclusive_i64_host. */
+int ki_scan_inclusive_i64_sharded_host(ki_comm* comm, const int64_t* h_in, int64_t* h_out, size_t n_local,
+                                       void* stream);
+/* filter/findall of the concatenated Float32 shards: rank r compacts its shard (ki_compact_gt_f32 with
+ * index_base = the 1-based global index of its first element for findall) into its own outputs; the
+ * counts are exchanged and *d_offset receives where rank r's kept elements start in the global result
+ * (the sum of the lower ranks' counts), *d_total the global count (device uint64; d_count, d_offset,
+ * d_total may be NULL).  The ranks' outputs concatenated in rank order are the global result. */
+int ki_compact_gt_f32_sharded(ki_comm* comm, const float* d_x, size_t n_local, float threshold, float* d_out_vals,
+                              int32_t* d_out_idx, int64_t index_base, uint64_t* d_count, uint64_t* d_offset,
+                              uint64_t* d_total, void* stream);
 
 /* ---- (a8) fp8 e4m3 GEMM on tcgen05 / TMEM ---------------------------------------------------
  * No counterpart in the reference.  C = (scale_a * scale_b) * A * B with A: M x K row-major e4m3,

@@ -29,9 +29,6 @@ namespace {
 #ifndef KI_COPY_WAVES
 #define KI_COPY_WAVES 2  // grid = whole waves of resident blocks
 #endif
-#ifndef KI_PIPE_CHUNK
-#define KI_PIPE_CHUNK (16u << 20)  // host-buffer copy: bytes per pipelined chunk
-#endif
 constexpr int kThreads = KI_COPY_THREADS;
 constexpr int kUnroll = KI_COPY_UNROLL;  // 32-chunk rows per warp span
 constexpr int kSpan = 32 * kUnroll;      // 16-byte chunks per warp span
@@ -146,7 +143,11 @@ int launch_vcopy(ki_ctx* ctx, void* dst, const void* src, size_t nbytes, cudaStr
     return launch_one<3, false>(ctx, a, want, 4, st);
 }
 
-int ensure_pipe(ki_ctx* ctx) {
+}  // namespace
+
+// Streams and events of the host-buffer pipelines (ki_vcopy_host, ki_scan_inclusive_i64_host), made
+// on first use.
+int ki_ensure_pipe(ki_ctx* ctx) {
     if (ctx->pipe_end) return KI_OK;
     for (int i = 0; i < 3; ++i)
         if (!ctx->pipe_stream[i])
@@ -161,6 +162,8 @@ int ensure_pipe(ki_ctx* ctx) {
     KI_CUDA(ctx, cudaEventCreateWithFlags(&ctx->pipe_end, cudaEventDisableTiming));  // last: marks "complete"
     return KI_OK;
 }
+
+namespace {
 
 bool overlap(uintptr_t d0, uintptr_t s0, size_t n) { return d0 < s0 + n && s0 < d0 + n; }
 
@@ -187,7 +190,7 @@ extern "C" int ki_vcopy_host(ki_ctx* ctx, void* dst, const void* src, size_t nby
     if (overlap((uintptr_t)dst, (uintptr_t)src, nbytes))
         return ki::set_error(ctx, KI_ERR_ARG, "vcopy_host: source and destination overlap");
     KI_GUARD(ctx);
-    int rc = ensure_pipe(ctx);
+    int rc = ki_ensure_pipe(ctx);
     if (rc) return rc;
     constexpr size_t kChunk = KI_PIPE_CHUNK;
     constexpr size_t kSlot = kChunk + 256;

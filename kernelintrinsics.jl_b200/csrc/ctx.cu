@@ -17,6 +17,7 @@ const char* ki_status_string(int status) {
         case KI_ERR_TIMEOUT: return "KI_ERR_TIMEOUT: a bounded device-side wait ran out";
         case KI_ERR_UNSUPPORTED: return "KI_ERR_UNSUPPORTED: device or feature not supported";
         case KI_ERR_NOMEM: return "KI_ERR_NOMEM: scratch allocation failed";
+        case KI_ERR_NCCL: return "KI_ERR_NCCL: an NCCL call failed";
         default: return "unknown ki_status";
     }
 }
@@ -99,7 +100,11 @@ int ki_ctx_destroy(ki_ctx* ctx) {
     return KI_OK;
 }
 
-const char* ki_last_error_string(const ki_ctx* ctx) { return ctx ? ctx->last_error : "null context"; }
+const char* ki_last_error_string(const ki_ctx* ctx) {
+    if (ctx) return ctx->last_error;
+    const char* t = ki::thread_error();
+    return t[0] ? t : "null context";
+}
 
 int ki_ctx_set_wait_timeout_ns(ki_ctx* ctx, uint64_t ns) {
     KI_CHECK_CTX(ctx);

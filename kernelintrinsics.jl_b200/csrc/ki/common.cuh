@@ -9,12 +9,7 @@
 #include <mutex>
 
 #include "../../../include/ki_b200.h"
-
-// Device status bits latched by kernels (read and cleared by ki_ctx_check).
-enum : uint32_t {
-    KI_DEV_TIMEOUT = 1u,      // a bounded wait ran out
-    KI_DEV_BAD_STATE = 2u,    // a kernel saw an impossible value (e.g. a corrupt tile flag)
-};
+#include "../../../include/ki/status.h"  // device status bits (read and cleared by ki_ctx_check)
 
 // Scratch regions, one per operation so different operations never share memory.
 enum ki_region {
@@ -26,11 +21,17 @@ enum ki_region {
     KI_REG_SCAN_ANY = 5,  // the generic scan (any operator and type)
     KI_REG_ROWS = 6,       // per-row tickets of the segmented reduce
     KI_REG_ROWS_PART = 7,  // per-row partials of the segmented reduce
-    KI_REG_COUNT = 8
+    KI_REG_HOST_SHARD = 8, // device copy of a shard for the two-phase sharded host-buffer scan
+    KI_REG_HOST_PART = 9,  // per-chunk totals of that scan
+    KI_REG_COUNT = 10
 };
 
-// Host-buffer copy pipeline: slots of staging memory cycled over three streams.
+// Host-buffer pipelines: slots of staging memory cycled over three streams (host -> device,
+// kernel, device -> host), KI_PIPE_CHUNK bytes per chunk.
 constexpr int KI_PIPE_SLOTS = 4;
+#ifndef KI_PIPE_CHUNK
+#define KI_PIPE_CHUNK (16u << 20)
+#endif
 
 struct ki_ctx {
     int device = 0;
@@ -53,6 +54,13 @@ struct ki_ctx {
 };
 
 namespace ki {
+
+// Message of the calling thread's last failed call that had no context to hold it (a communicator
+// whose set-up failed); ki_last_error_string(NULL) returns it.
+inline char* thread_error() {
+    static thread_local char buf[512] = {0};
+    return buf;
+}
 
 inline int set_error(ki_ctx* ctx, int status, const char* fmt, ...) {
     if (ctx) {
@@ -118,6 +126,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 }  // namespace ki
+
+// Streams and events of the host-buffer pipelines (copy.cu), made on first use.
+__attribute__((visibility("hidden"))) int ki_ensure_pipe(ki_ctx* ctx);
 
 #define KI_CHECK_CTX(ctx)                                              \
     do {                                                               \

@@ -70,6 +70,7 @@ struct ScanArgs {
     int64_t* out;
     size_t n;
     int64_t seed;
+    const int64_t* seed_ptr;  // when set, the seed is read from device memory at the start
     ki::TileStatus st;
     unsigned long long* ticket;
     uint32_t* status;
@@ -99,6 +100,8 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
     const int w = tid >> 5;
     const unsigned lane = tid & 31;
     const uint64_t ntiles = (a.n + kTile - 1) / kTile;
+    // only tile 0 uses the seed (its inclusive prefix is seed + aggregate; lookbacks stop there)
+    const int64_t seed = a.seed_ptr ? *a.seed_ptr : a.seed;
     auto bulk_ok = [&](uint64_t t) { return a.tma_in && t < ntiles && (t + 1) * (uint64_t)kTile <= a.n; };
     auto fetch = [&]() {  // take a ticket and start its load (one thread)
         const unsigned long long t = atomicAdd(a.ticket, 1ull);
@@ -128,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
         if (w == kLookWarp) {
             if (have_old) {
                 Pending& o = slot[cur ^ 1];
-                const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, a.seed, a.status,
+                const int64_t ex = ki::decoupled_lookback<kLookbackK>(a.st, o.t, o.agg, seed, a.status,
                                                                       a.timeout_ns);
                 if (lane == 0) o.tile_excl = ex;
             }
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
                 if (lane == 0) {
                     e.t = t_new;
                     e.agg = agg;
-                    ki::publish_aggregate(a.st, t_new, agg, a.seed);
+                    ki::publish_aggregate(a.st, t_new, agg, seed);
                 }
             }
         }
@@ -220,13 +223,16 @@ void launch_scan(const ScanArgs& a, size_t ntiles, int sm_count, cudaStream_t s)
 
 }  // namespace
 
-extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
-                                     void* stream) {
+namespace {
+
+int scan_i64_ctx(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed, const int64_t* d_seed,
+                 cudaStream_t s) {
     KI_CHECK_CTX(ctx);
     if (n == 0) return KI_OK;
     if (!d_in || !d_out) return ki::set_error(ctx, KI_ERR_ARG, "scan: null pointer");
     if (!ki::aligned(d_in, 8) || !ki::aligned(d_out, 8))
         return ki::set_error(ctx, KI_ERR_ARG, "scan: Int64 pointers must be 8-byte aligned");
+    if (d_seed && !ki::aligned(d_seed, 8)) return ki::set_error(ctx, KI_ERR_ARG, "scan: misaligned seed");
     if (d_in != d_out) {
         const uintptr_t i0 = (uintptr_t)d_in, o0 = (uintptr_t)d_out, nb = n * sizeof(int64_t);
         if (i0 < o0 + nb && o0 < i0 + nb)
@@ -242,7 +248,6 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     int rc = ki::ensure_region(ctx, KI_REG_SCAN, bytes, &base);
     if (rc) return rc;
     char* b = static_cast<char*>(base);
-    cudaStream_t s = ki::as_stream(stream);
     KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * sizeof(uint64_t), s));
 
     KI_CUDA(ctx, cudaFuncSetAttribute(scan_i64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -252,6 +257,7 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     a.out = d_out;
     a.n = n;
     a.seed = seed;
+    a.seed_ptr = d_seed;
     a.st.words = reinterpret_cast<uint64_t*>(b + words_off);
     a.st.aggs = reinterpret_cast<int64_t*>(b + words_off + ntiles * 8);
     a.st.incls = reinterpret_cast<int64_t*>(b + words_off + ntiles * 16);
@@ -262,6 +268,77 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     a.vec_out = ki::aligned(d_out, 16);
     launch_scan(a, ntiles, ctx->sm_count, s);
     return ki::check_launch(ctx, "scan_i64_kernel launch");
+}
+
+}  // namespace
+
+extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed,
+                                     void* stream) {
+    return scan_i64_ctx(ctx, d_in, d_out, n, seed, nullptr, ki::as_stream(stream));
+}
+
+extern "C" int ki_scan_inclusive_i64_dseed(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n,
+                                           const int64_t* d_seed, void* stream) {
+    KI_CHECK_CTX(ctx);
+    if (!d_seed) return ki::set_error(ctx, KI_ERR_ARG, "scan: null seed pointer");
+    return scan_i64_ctx(ctx, d_in, d_out, n, 0, d_seed, ki::as_stream(stream));
+}
+
+// Inclusive scan of HOST buffers through the device.  Chunks of KI_PIPE_CHUNK bytes go host ->
+// device on pipe stream 0, are scanned on stream 1 and come back on stream 2, cycling over
+// KI_PIPE_SLOTS staging slots (the pipeline of ki_vcopy_host), so both copy directions and the scans
+// overlap.  Chunk i > 0 is seeded on the device with the last output of chunk i-1, which is still in
+// its staging slot: that slot is rewritten only by chunk i-1+KI_PIPE_SLOTS, whose scan runs after
+// chunk i's on the same stream.
+extern "C" int ki_scan_inclusive_i64_host(ki_ctx* ctx, const int64_t* h_in, int64_t* h_out, size_t n, int64_t seed,
+                                          void* stream) {
+    KI_CHECK_CTX(ctx);
+    if (n == 0) return KI_OK;
+    if (!h_in || !h_out) return ki::set_error(ctx, KI_ERR_ARG, "scan_host: null pointer");
+    if (!ki::aligned(h_in, 8) || !ki::aligned(h_out, 8))
+        return ki::set_error(ctx, KI_ERR_ARG, "scan_host: Int64 pointers must be 8-byte aligned");
+    if (h_in != h_out) {
+        const uintptr_t i0 = (uintptr_t)h_in, o0 = (uintptr_t)h_out, nb = n * sizeof(int64_t);
+        if (i0 < o0 + nb && o0 < i0 + nb)
+            return ki::set_error(ctx, KI_ERR_ARG, "scan_host: partially overlapping input and output");
+    }
+    KI_GUARD(ctx);
+    int rc = ki_ensure_pipe(ctx);
+    if (rc) return rc;
+    constexpr size_t kChunk = KI_PIPE_CHUNK / sizeof(int64_t);  // elements per chunk
+    void* stage = nullptr;
+    rc = ki::ensure_region(ctx, KI_REG_STAGE, 2 * KI_PIPE_SLOTS * (size_t)KI_PIPE_CHUNK, &stage);
+    if (rc) return rc;
+    int64_t* base = static_cast<int64_t*>(stage);
+    cudaStream_t s = ki::as_stream(stream);
+    cudaStream_t up = ctx->pipe_stream[0], kern = ctx->pipe_stream[1], down = ctx->pipe_stream[2];
+    KI_CUDA(ctx, cudaEventRecord(ctx->pipe_begin, s));
+    for (int i = 0; i < 3; ++i) KI_CUDA(ctx, cudaStreamWaitEvent(ctx->pipe_stream[i], ctx->pipe_begin, 0));
+    const size_t nch = (n + kChunk - 1) / kChunk;
+    const int64_t* prev_last = nullptr;
+    for (size_t i = 0; i < nch; ++i) {
+        const int k = (int)(i % KI_PIPE_SLOTS);
+        const size_t off = i * kChunk, len = (n - off < kChunk) ? n - off : kChunk;
+        int64_t* in = base + (size_t)k * kChunk;
+        int64_t* out = base + (size_t)(KI_PIPE_SLOTS + k) * kChunk;
+        if (i >= (size_t)KI_PIPE_SLOTS) {
+            KI_CUDA(ctx, cudaStreamWaitEvent(up, ctx->pipe_copied[k], 0));     // input slot read
+            KI_CUDA(ctx, cudaStreamWaitEvent(kern, ctx->pipe_drained[k], 0));  // output slot sent back
+        }
+        KI_CUDA(ctx, cudaMemcpyAsync(in, h_in + off, len * sizeof(int64_t), cudaMemcpyHostToDevice, up));
+        KI_CUDA(ctx, cudaEventRecord(ctx->pipe_landed[k], up));
+        KI_CUDA(ctx, cudaStreamWaitEvent(kern, ctx->pipe_landed[k], 0));
+        rc = scan_i64_ctx(ctx, in, out, len, seed, prev_last, kern);
+        if (rc) return rc;
+        KI_CUDA(ctx, cudaEventRecord(ctx->pipe_copied[k], kern));
+        KI_CUDA(ctx, cudaStreamWaitEvent(down, ctx->pipe_copied[k], 0));
+        KI_CUDA(ctx, cudaMemcpyAsync(h_out + off, out, len * sizeof(int64_t), cudaMemcpyDeviceToHost, down));
+        KI_CUDA(ctx, cudaEventRecord(ctx->pipe_drained[k], down));
+        prev_last = out + len - 1;
+    }
+    KI_CUDA(ctx, cudaEventRecord(ctx->pipe_end, down));
+    KI_CUDA(ctx, cudaStreamWaitEvent(s, ctx->pipe_end, 0));
+    return KI_OK;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -275,9 +352,20 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
 //
 // The array is sized for KI_SCAN_NOALLOC_MAX_N elements (a 256-byte header plus three 8-byte words
 // per tile: 16,913 tiles of 15872 elements, about 397 KiB).  Every GPU that loads this library
-// holds it until the process exits.  In host code the array's name is only a host-side stand-in, so its device address
-// is looked up once per device with cudaGetSymbolAddress (with that device current) and cached; the
-// first call on each device does this set-up and must therefore come before any stream capture.
+// holds it until the process exits.
+//
+// In host code the array's name is only a host-side stand-in, so its device address is looked up
+// with cudaGetSymbolAddress (with the caller's device current) and cached.  A __device__ array's
+// address belongs to a CUDA context, not to a device, so the cache is keyed by the unique ID of the
+// calling thread's current context (cuCtxGetId): a call from a context not seen before (another
+// device, a non-primary context, a primary context re-created after cudaDeviceReset) repeats the
+// set-up.  The set-up runs, once per context: cudaGetSymbolAddress (which also loads the module
+// under lazy loading), cudaDeviceGetAttribute (SM count) and cudaFuncSetAttribute (dynamic shared
+// memory).  Every call also runs cudaFree(NULL) (frees nothing; makes the device's primary context
+// current if no context is), cuCtxGetCurrent and cuCtxGetId (reached through
+// cudaGetDriverEntryPointByVersion, so the library does not link libcuda).  Make the first call in
+// each context before any stream capture.
+//
 // All calls share the array and it keeps the last call's contents: each call clears the ticket, the
 // status word and the tile status words (cudaMemsetAsync on the cached address) before its launch,
 // and calls that overlap on the GPU (different streams, or several host threads) race on it.
@@ -290,13 +378,43 @@ constexpr size_t kNoAllocTiles = (KI_SCAN_NOALLOC_MAX_N + kTile - 1) / kTile;
 constexpr size_t kNoAllocHeader = 256;  // ticket at 0, status word at 64
 static __device__ __align__(256) unsigned char g_scan_noalloc_scratch[kNoAllocHeader + kNoAllocTiles * 24];
 
-struct NoAllocDevice {
-    bool ready = false;
+struct NoAllocContext {
+    unsigned long long ctx_id = 0;  // cuCtxGetId of the context the address belongs to (0: free slot)
     unsigned char* scratch = nullptr;
     int sm_count = 0;
 };
+constexpr int kNoAllocContexts = 64;
 std::mutex g_noalloc_mutex;
-NoAllocDevice g_noalloc_dev[64];
+NoAllocContext g_noalloc_ctx[kNoAllocContexts];
+int g_noalloc_next = 0;  // slot taken by the next new context (round robin once all are used)
+
+typedef int (*CtxGetCurrentFn)(void** ctx);                   // cuCtxGetCurrent
+typedef int (*CtxGetIdFn)(void* ctx, unsigned long long* id);  // cuCtxGetId
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+// Unique ID of the calling thread's current CUDA context, 0 on failure.  Called with the mutex held.
+unsigned long long current_context_id() {
+    if (!g_ctx_get_current || !g_ctx_get_id) {
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f1, 12000, cudaEnableDefault, &q1) != cudaSuccess ||
+            q1 != cudaDriverEntryPointSuccess || !f1)
+            return 0;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f2, 12000, cudaEnableDefault, &q2) != cudaSuccess ||
+            q2 != cudaDriverEntryPointSuccess || !f2)
+            return 0;
+        g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+        g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
+    }
+    if (cudaFree(nullptr) != cudaSuccess) return 0;  // frees nothing; binds the primary context if none is current
+    void* c = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_get_current(&c) != 0 || !c) return 0;
+    if (g_ctx_get_id(c, &id) != 0) return 0;
+    return id;
+}
 
 }  // namespace
 
@@ -310,26 +428,33 @@ extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out
         const uintptr_t i0 = (uintptr_t)d_in, o0 = (uintptr_t)d_out, nb = n * sizeof(int64_t);
         if (i0 < o0 + nb && o0 < i0 + nb) return KI_ERR_ARG;
     }
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KI_ERR_CUDA;
     unsigned char* scratch = nullptr;
     int sm_count = 0;
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-        NoAllocDevice& d = g_noalloc_dev[dev];
-        if (!d.ready) {
+        const unsigned long long id = current_context_id();
+        if (id == 0) return KI_ERR_CUDA;
+        NoAllocContext* c = nullptr;
+        for (auto& e : g_noalloc_ctx)
+            if (e.ctx_id == id) c = &e;
+        if (!c) {  // first call in this context: look the array up and prepare the kernel
+            int dev = -1, sms = 0;
             void* p = nullptr;
+            if (cudaGetDevice(&dev) != cudaSuccess) return KI_ERR_CUDA;
             if (cudaGetSymbolAddress(&p, g_scan_noalloc_scratch) != cudaSuccess || !p) return KI_ERR_CUDA;
-            if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
                 return KI_ERR_CUDA;
             if (cudaFuncSetAttribute(scan_i64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kSmemBytes) != cudaSuccess)
                 return KI_ERR_CUDA;
-            d.scratch = static_cast<unsigned char*>(p);
-            d.ready = true;
+            c = &g_noalloc_ctx[g_noalloc_next];
+            g_noalloc_next = (g_noalloc_next + 1) % kNoAllocContexts;
+            c->ctx_id = id;
+            c->scratch = static_cast<unsigned char*>(p);
+            c->sm_count = sms;
         }
-        scratch = d.scratch;
-        sm_count = d.sm_count;
+        scratch = c->scratch;
+        sm_count = c->sm_count;
     }
     const size_t ntiles = (n + kTile - 1) / kTile;
     cudaStream_t s = ki::as_stream(stream);
@@ -340,6 +465,7 @@ extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out
     a.out = d_out;
     a.n = n;
     a.seed = seed;
+    a.seed_ptr = nullptr;
     a.st.words = reinterpret_cast<uint64_t*>(scratch + kNoAllocHeader);
     a.st.aggs = reinterpret_cast<int64_t*>(scratch + kNoAllocHeader + kNoAllocTiles * 8);
     a.st.incls = reinterpret_cast<int64_t*>(scratch + kNoAllocHeader + kNoAllocTiles * 16);
@@ -348,6 +474,12 @@ extern "C" int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out
     a.timeout_ns = 2000000000ull;
     a.tma_in = ki::aligned(d_in, 16);
     a.vec_out = ki::aligned(d_out, 16);
-    launch_scan(a, ntiles, sm_count, s);
-    return cudaGetLastError() == cudaSuccess ? KI_OK : KI_ERR_CUDA;
+    // cudaLaunchKernel returns this launch's own status: an earlier, unrelated error left in the
+    // runtime's last-error slot is neither returned nor cleared.
+    size_t grid = (size_t)sm_count * kCtasPerSm;
+    if (grid > ntiles) grid = ntiles;
+    void* args[] = {&a};
+    const cudaError_t e =
+        cudaLaunchKernel((const void*)scan_i64_kernel, dim3((unsigned)grid), dim3(kThreads), args, kSmemBytes, s);
+    return e == cudaSuccess ? KI_OK : KI_ERR_CUDA;
 }

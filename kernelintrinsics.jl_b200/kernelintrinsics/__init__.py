@@ -30,7 +30,7 @@ __all__ = [
     "Up", "Down", "Xor", "Idx", "All", "AnyLane", "Uni", "Ballot", "KIError", "KIArgumentError",
     "KITimeoutError", "Context", "context", "warpsize", "get_warpsize", "devices", "shfl", "warpreduce",
     "warpfold", "vote", "vload", "vstore", "vload_multi", "vstore_multi", "generate_partN", "access",
-    "message_pass", "vcopy", "vcopy_host", "reduce", "reduce_rows", "scan", "compact", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "vote_compact",
+    "message_pass", "vcopy", "vcopy_host", "reduce", "reduce_rows", "scan", "compact", "warpfold_reduce", "reduce_sum_i64", "warpreduce_scan", "warpreduce_scan_host", "vote_compact",
     "fp8_gemm", "fill_uniform", "fill_int_range", "fill_bytes", "fill_normal", "fill_e4m3_uniform",
 ]
 
@@ -548,6 +548,21 @@ def warpreduce_scan(x, out=None, seed: int = 0, stream=None):
     out = torch.empty_like(x) if out is None else out
     context(d).call("ki_scan_inclusive_i64", _ptr(x), _ptr(out), x.numel(), ctypes.c_int64(int(seed)),
                     _stream_ptr(stream, d))
+    return out
+
+
+def warpreduce_scan_host(x, out=None, seed: int = 0, device: int = 0, stream=None):
+    """cumsum of a HOST Int64 tensor through GPU ``device`` (chunks cross PCIe, are scanned there and come
+    back, both directions overlapped).  Pinned tensors make it asynchronous; it is complete when
+    ``stream`` (of ``device``) is."""
+    torch = _torch()
+    if x.is_cuda or x.dtype != torch.int64 or not x.is_contiguous():
+        raise KIArgumentError(_abi.KI_ERR_ARG, "warpreduce_scan_host: contiguous Int64 host tensor")
+    out = torch.empty_like(x) if out is None else out
+    if out.is_cuda or out.dtype != torch.int64 or out.numel() != x.numel() or not out.is_contiguous():
+        raise KIArgumentError(_abi.KI_ERR_ARG, "warpreduce_scan_host: output must match the input, on the host")
+    context(device).call("ki_scan_inclusive_i64_host", _ptr(x), _ptr(out), x.numel(), ctypes.c_int64(int(seed)),
+                         _stream_ptr(stream, device))
     return out
 
 

@@ -13,7 +13,9 @@ PKG_ROOT = Path(__file__).resolve().parent.parent          # kernelintrinsics.jl
 LIB_PATH = PKG_ROOT / "lib" / "libki_b200.so"
 
 # ki_status
-KI_OK, KI_ERR_ARG, KI_ERR_CUDA, KI_ERR_TIMEOUT, KI_ERR_UNSUPPORTED, KI_ERR_NOMEM = range(6)
+KI_OK, KI_ERR_ARG, KI_ERR_CUDA, KI_ERR_TIMEOUT, KI_ERR_UNSUPPORTED, KI_ERR_NOMEM, KI_ERR_NCCL = range(7)
+KI_XCHG_AUTO, KI_XCHG_PEER, KI_XCHG_NCCL = range(3)
+COMM_ID_BYTES = 128
 
 # enums (include/ki_b200.h)
 SCOPE = {"default": 0, "workgroup": 1, "device": 2, "system": 3}
@@ -49,6 +51,21 @@ SIGNATURES = {
     "ki_reduce_sum_f32": (_i32, [_vp, _vp, _sz, _vp, _vp, _vp]),
     "ki_reduce_sum_i64": (_i32, [_vp, _vp, _sz, _vp, _vp]),
     "ki_scan_inclusive_i64": (_i32, [_vp, _vp, _vp, _sz, _i64, _vp]),
+    "ki_scan_inclusive_i64_dseed": (_i32, [_vp, _vp, _vp, _sz, _vp, _vp]),
+    "ki_scan_inclusive_i64_host": (_i32, [_vp, _vp, _vp, _sz, _i64, _vp]),
+    "ki_scan_inclusive_i64_sharded_host": (_i32, [_vp, _vp, _vp, _sz, _vp]),
+    "ki_comm_shard_range": (_i32, [_sz, _i32, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
+    "ki_comm_get_id": (_i32, [_vp]),
+    "ki_comm_init_rank": (_i32, [_i32, _i32, _i32, _vp, _i32, ctypes.POINTER(_vp)]),
+    "ki_comm_create": (_i32, [_i32, ctypes.POINTER(_i32), ctypes.POINTER(_vp)]),
+    "ki_comm_destroy": (_i32, [_vp]),
+    "ki_comm_abort": (_i32, [_vp]),
+    "ki_comm_info": (_i32, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                            ctypes.POINTER(_i32)]),
+    "ki_comm_get_ctx": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "ki_reduce_sum_f32_sharded": (_i32, [_vp, _vp, _sz, _vp, _vp, _vp]),
+    "ki_scan_inclusive_i64_sharded": (_i32, [_vp, _vp, _vp, _sz, _vp]),
+    "ki_compact_gt_f32_sharded": (_i32, [_vp, _vp, _sz, _f32, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "ki_reduce": (_i32, [_vp, _i32, _i32, _vp, _sz, _vp, _vp]),
     "ki_compact": (_i32, [_vp, _i32, _i32, _vp, _sz, _vp, _vp, _vp, _i64, _vp, _vp]),
     "ki_reduce_rows": (_i32, [_vp, _i32, _i32, _vp, _sz, _sz, _sz, _vp, _vp]),

@@ -1,7 +1,11 @@
-"""GPU, 2+ devices: range-sharded reduce / scan / compaction over NCCL against the oracle.
+"""GPU, 2+ devices: the C-ABI communicator's sharded reduce / scan / compaction against the oracle.
 
-Each rank owns a contiguous shard; only one 8-byte value per rank crosses NVLink (an all-gather of
-shard totals or counts).  Skipped when fewer than 2 GPUs are visible.
+Each rank owns a contiguous shard; only one 8-byte value per rank and operation crosses NVLink.
+Two ways to drive the GPUs are tested: one process driving all of them (ki_comm_create) and one
+process per GPU (ki_comm_init_rank, with the peer exchange and with the NCCL fallback exchange).
+A rank that leaves between steps makes the other ranks' next exchange time out (bounded device
+wait, KI_ERR_TIMEOUT), after which they abort.  Skipped when fewer GPUs are visible.
+NVLS is off in every child (NCCL_NVLS_ENABLE=0) and no multicast object is used.
 """
 from __future__ import annotations
 
@@ -13,6 +17,8 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
+N_SCAN, N_CMP, N_SUM = (1 << 22) + 12345, (1 << 21) + 777, (1 << 22) + 3
+
 
 def _free_port():
     with socket.socket() as s:
@@ -20,83 +26,213 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, n_scan, n_cmp, results):
+def _need(world):
+    import torch
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+def _inputs(KI, dev):
+    """The whole inputs on one device (counter-based generators: every rank makes the same arrays)."""
+    import torch
+
+    xi = torch.empty(N_SCAN, dtype=torch.int64, device=dev)
+    KI.fill_int_range(xi, seed=3, lo=-1000, hi=1000)
+    xf = torch.empty(N_SUM, dtype=torch.float32, device=dev)
+    KI.fill_uniform(xf, seed=1)
+    xn = torch.empty(N_CMP, dtype=torch.float32, device=dev)
+    KI.fill_normal(xn, seed=4)
+    return xi, xf, xn
+
+
+def _check(oracle, world, sums, scans, vals, idxs, counts, offs, totals, xn_host):
+    xi = oracle.gen_int_range_i64(3, -1000, 1000, N_SCAN)
+    ref_sum = oracle.sum_f32(oracle.gen_uniform_f32(1, N_SUM))
+    assert len(set(sums)) == 1  # every rank holds the same bits
+    assert abs(sums[0] - ref_sum) <= 1e-5 * np.log2(N_SUM) * ref_sum
+    assert np.array_equal(np.concatenate(scans), oracle.cumsum_i64(xi))
+    rv, ri = oracle.filter_gt_f32(xn_host, 0.5)
+    assert np.array_equal(np.concatenate(vals), rv) and np.array_equal(np.concatenate(idxs), ri)
+    assert offs == [int(sum(counts[:r])) for r in range(world)]
+    assert all(t == rv.size for t in totals)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_ops_single_process(world, KI, oracle):
+    """One host thread drives `world` GPUs through ki_comm_create; two rounds (both buffer parities)."""
+    import torch
+
+    from kernelintrinsics import sharded
+
+    _need(world)
+    comms = sharded.Comm.create(list(range(world)))
+    try:
+        per = []
+        for r, c in enumerate(comms):
+            dev = torch.device("cuda", r)
+            xi, xf, xn = _inputs(KI, dev)
+            lo, hi = c.shard_range(N_SCAN)
+            slo, shi = c.shard_range(N_SUM)
+            clo, chi = c.shard_range(N_CMP)
+            per.append((xi[lo:hi].contiguous(), xf[slo:shi].contiguous(), xn[clo:chi].contiguous(), clo))
+            torch.cuda.synchronize(dev)
+        for _ in range(2):
+            outs = []
+            for c, (xi, xf, xn, clo) in zip(comms, per):  # enqueue every rank before waiting on any
+                with torch.cuda.device(c.device):
+                    outs.append((c.reduce_sum(xf), c.scan(xi), c.compact_gt(xn, 0.5, index_base=1 + clo)))
+            for c in comms:
+                c.check()
+            sums = [o[0].item() for o in outs]
+            scans = [o[1].cpu().numpy() for o in outs]
+            counts = [int(o[2][2].item()) for o in outs]
+            vals = [o[2][0][:k].cpu().numpy() for o, k in zip(outs, counts)]
+            idxs = [o[2][1][:k].cpu().numpy() for o, k in zip(outs, counts)]
+            offs = [int(o[2][3].item()) for o in outs]
+            totals = [int(o[2][4].item()) for o in outs]
+            xn_host = _inputs(KI, torch.device("cuda", 0))[2].cpu().numpy()
+            _check(oracle, world, sums, scans, vals, idxs, counts, offs, totals, xn_host)
+    finally:
+        for c in comms:
+            c.close()
+
+
+def _worker(rank, world, port, exchange, results):
     import datetime
     import sys
     from pathlib import Path
 
     repo = Path(__file__).resolve().parent.parent
     sys.path.insert(0, str(repo / "kernelintrinsics.jl_b200"))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
-                            device_id=torch.device("cuda", rank))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    comm = None
     try:
         import kernelintrinsics as KI
         from kernelintrinsics import sharded
 
+        comm = sharded.Comm.from_process_group(device=rank, exchange=exchange)
         dev = torch.device("cuda", rank)
-        # the whole inputs are generated on every rank (same stream), each rank keeps its shard
-        xi = torch.empty(n_scan, dtype=torch.int64, device=dev)
-        KI.fill_int_range(xi, seed=3, lo=-1000, hi=1000)
-        xf = torch.empty(n_scan, dtype=torch.float32, device=dev)
-        KI.fill_uniform(xf, seed=1)
-        xn = torch.empty(n_cmp, dtype=torch.float32, device=dev)
-        KI.fill_normal(xn, seed=4)
-        lo, hi = sharded.shard_range(n_scan, world, rank)
-        clo, chi = sharded.shard_range(n_cmp, world, rank)
-        tot = sharded.reduce_sharded(xf[lo:hi])
-        sc = sharded.scan_sharded(xi[lo:hi].contiguous())
-        v, i, k, off, total = sharded.compact_sharded(xn[clo:chi].contiguous(), 0.5, clo)
-        KI.context(rank).check()
+        xi, xf, xn = _inputs(KI, dev)
+        lo, hi = comm.shard_range(N_SCAN)
+        slo, shi = comm.shard_range(N_SUM)
+        clo, chi = comm.shard_range(N_CMP)
+        res = []
+        for _ in range(2):
+            tot = comm.reduce_sum(xf[slo:shi].contiguous())
+            sc = comm.scan(xi[lo:hi].contiguous())
+            v, i, c, off, total = comm.compact_gt(xn[clo:chi].contiguous(), 0.5, index_base=1 + clo)
+            comm.check()
+            k = int(c.item())
+            res.append((float(tot.item()), sc.cpu().numpy().tobytes(), v[:k].cpu().numpy().tobytes(),
+                        i[:k].cpu().numpy().tobytes(), k, int(off.item()), int(total.item())))
+        # the same scan with the shard in pinned host memory (two-phase host-buffer path)
+        xh = xi[lo:hi].cpu().pin_memory()
+        yh = comm.scan_host(xh)
         torch.cuda.synchronize()
-        results[rank] = (float(tot), sc.cpu().numpy().tobytes(), v.cpu().numpy().tobytes(),
-                         i.cpu().numpy().tobytes(), k, off, total)
+        comm.check()
+        results[("host", rank)] = yh.numpy().tobytes()
+        results[rank] = (comm.exchange, res)
+        comm.close()
+        comm = None
     finally:
-        dist.barrier()
+        if comm is not None:
+            comm.abort()
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_sharded_ops_nccl(world, oracle):
+@pytest.mark.parametrize("world,exchange", [(2, "peer"), (2, "nccl"), (4, "auto"), (8, "auto")])
+def test_sharded_ops_process_per_gpu(world, exchange, KI, oracle):
     import torch
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    n_scan, n_cmp = (1 << 22) + 12345, (1 << 21) + 777
+    _need(world)
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     results = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, n_scan, n_cmp, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, results)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(300)
         assert p.exitcode == 0
-    xi = oracle.gen_int_range_i64(3, -1000, 1000, n_scan)
-    xf = oracle.gen_uniform_f32(1, n_scan)
-    ref_sum = oracle.sum_f32(xf)
-    sums = [results[r][0] for r in range(world)]
-    assert len(set(sums)) == 1  # every rank holds the same bits
-    assert abs(sums[0] - ref_sum) <= 1e-9 * ref_sum
-    scan = np.concatenate([np.frombuffer(results[r][1], dtype=np.int64) for r in range(world)])
-    assert np.array_equal(scan, oracle.cumsum_i64(xi))
-    vals = np.concatenate([np.frombuffer(results[r][2], dtype=np.float32) for r in range(world)])
-    idx = np.concatenate([np.frombuffer(results[r][3], dtype=np.int32) for r in range(world)])
-    # the oracle runs on the device-generated normals (same seed on every rank)
-    xn = None
-    import torch as _t
-    import kernelintrinsics as KI
-    d = _t.empty(n_cmp, dtype=_t.float32, device="cuda:0")
-    KI.fill_normal(d, seed=4)
-    xn = d.cpu().numpy()
-    rv, ri = oracle.filter_gt_f32(xn, 0.5)
-    assert np.array_equal(vals, rv) and np.array_equal(idx, ri)
-    assert all(results[r][6] == rv.size for r in range(world))
+    xn_host = _inputs(KI, torch.device("cuda", 0))[2].cpu().numpy()
+    want_mode = "nccl" if exchange == "nccl" else "peer"
+    want_scan = oracle.cumsum_i64(oracle.gen_int_range_i64(3, -1000, 1000, N_SCAN))
+    got = np.concatenate([np.frombuffer(results[("host", r)], dtype=np.int64) for r in range(world)])
+    assert np.array_equal(got, want_scan)
+    for rnd in range(2):
+        rs = [results[r][1][rnd] for r in range(world)]
+        assert all(results[r][0] == want_mode for r in range(world))
+        _check(oracle, world, [x[0] for x in rs], [np.frombuffer(x[1], dtype=np.int64) for x in rs],
+               [np.frombuffer(x[2], dtype=np.float32) for x in rs], [np.frombuffer(x[3], dtype=np.int32) for x in rs],
+               [x[4] for x in rs], [x[5] for x in rs], [x[6] for x in rs], xn_host)
+
+
+def _leaver(rank, world, port, results):
+    """Rank 1 stops taking part between steps (nothing of it in flight) but stays alive, so its
+    exchange buffer stays mapped; rank 0's next exchange waits for it, runs out (0.2 s) and reports
+    KI_ERR_TIMEOUT.  Rank 1 exits only after rank 0 has aborted its communicator."""
+    import datetime
+    import sys
+    import time
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo / "kernelintrinsics.jl_b200"))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from kernelintrinsics import sharded
+
+    comm = sharded.Comm.from_process_group(device=rank, exchange="peer")
+    x = torch.ones(4096, dtype=torch.float32, device=torch.device("cuda", rank))
+    comm.reduce_sum(x)  # one good step together
+    comm.check()
+    dist.barrier()
+    if rank == 1:  # leaves the computation, not the process
+        deadline = time.time() + 120
+        while "after" not in results and time.time() < deadline:
+            time.sleep(0.05)
+        comm.abort()
+        os._exit(0)
+    comm.set_wait_timeout(0.2)
+    comm.reduce_sum(x)
+    try:
+        comm.check()
+        results[rank] = "no error"
+    except Exception as e:  # noqa: BLE001 - the timeout is the expected outcome
+        results[rank] = type(e).__name__
+    comm.abort()
+    results["after"] = x.sum().item()  # the device is still usable afterwards
+    os._exit(0)
+
+
+def test_rank_that_stops_is_detected(KI):
+    import torch.multiprocessing as mp
+
+    _need(2)
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert results.get(0) == "KITimeoutError"
+    assert results.get("after") == 4096.0

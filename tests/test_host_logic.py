@@ -155,3 +155,90 @@ def test_dead_rank_is_detected_on_host():
     for p in procs:
         p.join(120)
     assert results.get(0) not in (None, "no error")
+
+
+# ---------------------------------------------------------------------------------------------
+# the C-ABI communicator: host-only parts
+# ---------------------------------------------------------------------------------------------
+def test_c_shard_range_matches_python():
+    import ctypes
+
+    from kernelintrinsics import _abi
+
+    lib = _abi.load()
+    lo, cnt = ctypes.c_size_t(), ctypes.c_size_t()
+    for n in (0, 1, 7, 1000, 2**30 + 3, 2**28):
+        for world in (1, 2, 3, 8, 64):
+            for r in range(world):
+                assert lib.ki_comm_shard_range(n, world, r, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_OK
+                a, b = shard_range(n, world, r)
+                assert (lo.value, cnt.value) == (a, b - a)
+    assert lib.ki_comm_shard_range(10, 0, 0, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_ERR_ARG
+    assert lib.ki_comm_shard_range(10, 2, 2, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_ERR_ARG
+
+
+def test_comm_argument_checks_without_a_gpu():
+    """Invalid communicator arguments are rejected before any CUDA or NCCL call."""
+    import ctypes
+
+    from kernelintrinsics import _abi
+
+    lib = _abi.load()
+    h = ctypes.c_void_p()
+    cid = ctypes.create_string_buffer(128)
+    assert lib.ki_comm_init_rank(0, 0, 0, cid, 0, ctypes.byref(h)) == _abi.KI_ERR_ARG      # no ranks
+    assert lib.ki_comm_init_rank(0, 65, 0, cid, 0, ctypes.byref(h)) == _abi.KI_ERR_ARG     # > KI_COMM_MAX_RANKS
+    assert lib.ki_comm_init_rank(0, 2, 2, cid, 0, ctypes.byref(h)) == _abi.KI_ERR_ARG      # rank out of range
+    assert lib.ki_comm_init_rank(0, 2, 0, None, 0, ctypes.byref(h)) == _abi.KI_ERR_ARG     # no id
+    assert lib.ki_comm_init_rank(0, 2, 0, cid, 7, ctypes.byref(h)) == _abi.KI_ERR_ARG      # unknown exchange
+    devs = (ctypes.c_int * 1)(0)
+    hs = (ctypes.c_void_p * 1)()
+    assert lib.ki_comm_create(0, devs, hs) == _abi.KI_ERR_ARG
+    assert lib.ki_comm_destroy(None) == _abi.KI_OK and lib.ki_comm_abort(None) == _abi.KI_OK
+    assert lib.ki_reduce_sum_f32_sharded(None, None, 0, None, None, None) == _abi.KI_ERR_ARG
+    assert lib.ki_scan_inclusive_i64_sharded(None, None, None, 0, None) == _abi.KI_ERR_ARG
+    assert lib.ki_compact_gt_f32_sharded(None, None, 0, 0.5, None, None, 1, None, None, None, None) == _abi.KI_ERR_ARG
+    assert b"KI_ERR_NCCL" in lib.ki_status_string(_abi.KI_ERR_NCCL)
+
+
+def _id_worker(rank, world, port, results):
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo / "kernelintrinsics.jl_b200"))
+    from kernelintrinsics import sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        made = []
+
+        def make_id():
+            made.append(rank)
+            return bytes(range(128))
+
+        cid = sharded.broadcast_comm_id(make_id)
+        results[rank] = (cid, list(made))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_comm_id_broadcast_gloo(world):
+    """Rank 0 alone makes the NCCL unique id; every rank receives the same 128 bytes."""
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_id_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    for r in range(world):
+        cid, made = results[r]
+        assert cid == bytes(range(128))
+        assert made == ([0] if r == 0 else [])

@@ -2,13 +2,15 @@
 
 ki_scan_inclusive_i64_noalloc exists for callers that cannot allocate device memory (code running
 while a CUDA graph is captured, hosts whose device memory belongs to another allocator, loops that
-forbid allocation after start-up).  It must give exactly what the context-based entry point gives,
-on consecutive calls that share its static scratch.  This file is collected last on purpose.
+forbid allocation after start-up).  It must give exactly Base.cumsum (the oracle) and what the
+context-based entry point gives, on consecutive calls that share its static scratch.  This file is
+collected last on purpose.
 """
 from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
@@ -21,7 +23,7 @@ def _noalloc(lib, x, y, n, seed, stream):
                                              ctypes.c_int64(seed), ctypes.c_void_p(stream.cuda_stream))
 
 
-def test_noalloc_scan_matches_context_scan_twice(KI, dev):
+def test_noalloc_scan_matches_oracle_and_context_scan_twice(KI, dev, oracle):
     import torch
 
     from kernelintrinsics import _abi
@@ -32,11 +34,36 @@ def test_noalloc_scan_matches_context_scan_twice(KI, dev):
     for n, data_seed, seed in cases:  # two calls in a row on the shared static scratch
         x = torch.empty(n, dtype=torch.int64, device=dev)
         KI.fill_int_range(x, seed=data_seed, lo=-1000, hi=1000)
-        want = KI.warpreduce_scan(x, seed=seed)
+        want_ctx = KI.warpreduce_scan(x, seed=seed)
         got = torch.full_like(x, 7)
         assert _noalloc(lib, x, got, n, seed, stream) == _abi.KI_OK
         torch.cuda.synchronize()
-        assert torch.equal(got, want), n  # integer scan: bit-exact is the tolerance
+        want = oracle.cumsum_i64(oracle.gen_int_range_i64(data_seed, -1000, 1000, n), seed=seed)
+        got_h = got.cpu().numpy()
+        assert np.array_equal(got_h, want), n  # integer scan: bit-exact is the tolerance
+        assert torch.equal(got, want_ctx), n
+
+
+def test_noalloc_scan_at_its_largest_size(KI, dev):
+    """n just under the maximum fills nearly every tile slot of the static scratch; the output is
+    fixed exactly by out[0] = seed + in[0] and out[i] - out[i-1] = in[i] (checked on the device)."""
+    import torch
+
+    from kernelintrinsics import _abi
+
+    lib = _abi.load()
+    stream = torch.cuda.current_stream(dev)
+    n = MAX_N - 3
+    x = torch.empty(n, dtype=torch.int64, device=dev)
+    KI.fill_int_range(x, seed=5, lo=-1000, hi=1000)
+    y = torch.empty_like(x)
+    for seed in (0, 1 << 40):  # twice in a row
+        assert _noalloc(lib, x, y, n, seed, stream) == _abi.KI_OK
+        torch.cuda.synchronize()
+        assert int(y[0].item()) == seed + int(x[0].item())
+        assert torch.equal(y[1:] - y[:-1], x[1:])
+    del x, y
+    torch.cuda.empty_cache()
 
 
 def test_noalloc_scan_rejects_sizes_beyond_its_scratch(KI, dev):

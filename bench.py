@@ -1,19 +1,28 @@
 #!/usr/bin/env python
 """Benchmark of the KernelIntrinsics B200 primitives (one JSON line on rank 0).
 
-Headline workload: the vectorised byte copy (copyto!) of 2^28 bytes.  One step copies 2^28 bytes
-once for each of the 256 (src_offset, dst_offset) pairs in 0..15 x 0..15, so every step exercises
-every relative misalignment.  Every rank copies its own buffers (weak scaling, no collective).
+Headline workload: the Int64 inclusive prefix sum (Base.cumsum) of n = 2^30 elements drawn from
+U{-1000..1000}, split into contiguous shards over the N GPUs (strong scaling: the total is fixed).
+Each rank scans its shard through the libki_b200 communicator (ki_scan_inclusive_i64_sharded):
+phase 1 sums the shard, one 8-byte total per rank crosses NVLink (pushed into every peer's exchange
+buffer by the exchange kernel), phase 2 scans the shard seeded on the device.  The shards follow
+ki_comm_scan_shard_range (the last rank, which skips phase 1, holds 3/2 of a share so every rank
+moves the same bytes).  One step is one sharded scan of the whole array.
 
 The same line carries, under "kernels", the other device-wide primitives on their own workloads:
-  reduce   Float32 sum, n = 2^24 (L2 flushed between steps; inputs are smaller than L2)
-  scan     Int64 inclusive scan, n = 2^30, range-sharded over the ranks + NCCL all-gather of totals
-  scan_f32 Float32 cumsum (generic scan, Float64 accumulation), n = 2^28 per rank
-  compact  filter/findall of x > 0.5 over 2^28 N(0,1) Float32, range-sharded + all-gather of counts
+  copy     copyto! of 2^28 bytes, one step = 256 copies at every (src, dst) offset pair (weak
+           scaling: each rank copies its own buffers)
+  reduce   Float32 sum, n = 2^24 in total, sharded (8 rotating inputs, more than L2)
+  scan_f32 Float32 cumsum (generic scan, Float64 accumulation), n = 2^28 per rank (replicas)
+  compact  filter/findall of x > 0.5 over 2^28 N(0,1) Float32 in total, sharded
   gemm     fp8 e4m3 GEMM 8192^3 with Float32 output (replicas at N > 1)
+Outside every timed region each rank checks its results ("parity"): the scan against the oracle's
+cumsum on windows of the global input plus the difference property over the whole shard and the
+shard boundaries, the compaction against the oracle's filter/findall on the whole shard, the sum
+against the oracle's Float64 sum.  A mismatch makes the run exit non-zero.
 
---impl reference times the reference semantics' CPU implementation (the C oracle, all host
-threads) on the headline workload, rank 0 only.
+--impl reference times the reference semantics' CPU implementation (the C oracle's multithreaded
+cumsum, all host threads) on the headline workload, rank 0 only.
 
 Launch: python bench.py [--gpus N --steps K --warmup W]; N > 1 under torch.distributed.run.
 """
@@ -39,17 +48,29 @@ SCAN_N = 1 << 30
 SCAN_F32_N = 1 << 28
 COMPACT_N = 1 << 28
 GEMM_MNK = 8192
-L2_FLUSH_BYTES = 256 << 20
+GOLDEN = 0x9E3779B97F4A7C15  # splitmix64 increment: element i of stream s is mix64(s + (i+1)*GOLDEN)
 
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of the
-# headline kernel (ncu flushes L2 before the capture, so ~50 MB of the launch's writes are still in
-# L2 when it ends); the capture and its command are summarised in profiles/.
-NCU_TRAFFIC_PER_LAUNCH = {
-    "vcopy_kernel": 486_999_808,
-}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the headline kernel,
+# scan_i64_kernel: 1,035,870,000 B captured by ncu at n = 2^26 (profiles/scan_i64_kernel_2e26.md),
+# scaled by the elements a launch processes (the traffic grows in proportion: one read of the input,
+# one write of the output, ~8 B of tile status per 15872 elements).
+NCU_TRAFFIC_PER_ELEM = {"scan_i64_kernel": 1_035_870_000 / (1 << 26), "vcopy_kernel": 486_999_808 / (1 << 28)}
+
+SCAN_WORKLOAD = ("Int64 inclusive prefix sum (cumsum) of n=2^30 U{-1000..1000}, contiguous shards over the GPUs "
+                 "(ki_comm_scan_shard_range), shard totals exchanged over NVLink")
+
+
+def window_seed(seed: int, lo: int) -> int:
+    """Seed of the stream whose element i is element lo + i of stream ``seed`` (a shard's window)."""
+    return (seed + lo * GOLDEN) % (1 << 64)
+
+
+def wrap64(v: int) -> int:
+    v &= (1 << 64) - 1
+    return v - (1 << 64) if v >= 1 << 63 else v
 
 
 def parse():
@@ -58,7 +79,7 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--no-extra", action="store_true", help="headline copy only")
+    p.add_argument("--no-extra", action="store_true", help="headline scan only")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="", help="comma list of kernels to run under 'kernels'")
@@ -178,15 +199,12 @@ def run_profile(args):
 # ---------------------------------------------------------------------------------------------
 class Dist:
     def __init__(self, gpus: int):
-        import torch
-
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         if self.world != gpus and not (self.world == 1 and gpus == 1):
             raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}")
         self.dev = self.local
-        self.pg = None
 
     def init(self):
         import datetime
@@ -198,7 +216,6 @@ class Dist:
         if self.world > 1:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.dev))
-            self.pg = True
 
     def barrier(self):
         import torch
@@ -208,15 +225,24 @@ class Dist:
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max(self, v: float) -> float:
+    def gather(self, v) -> list:
+        """Every rank's Python number (int64 or float64), in rank order."""
         import torch
         import torch.distributed as dist
 
         if self.world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+            return [v]
+        dt = torch.float64 if isinstance(v, float) else torch.int64
+        t = torch.tensor([v], dtype=dt, device="cuda")
+        out = torch.empty(self.world, dtype=dt, device="cuda")
+        dist.all_gather_into_tensor(out, t)
+        return [x.item() for x in out.cpu()]
+
+    def max(self, v: float) -> float:
+        return max(self.gather(float(v)))
+
+    def all_ok(self, ok: bool) -> bool:
+        return min(self.gather(int(bool(ok)))) == 1
 
     def close(self):
         import torch.distributed as dist
@@ -293,102 +319,165 @@ def roofline(bound, achieved, peak, unit, traffic, source):
             "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": source}
 
 
-# ---------------------------------------------------------------------------------------------
-# headline: byte copy over the 256 (src_offset, dst_offset) pairs
-# ---------------------------------------------------------------------------------------------
-PAIRS = [(so, do) for do in range(16) for so in range(16)]
+def oracle_mod():
+    """The oracle (C restatement of the reference semantics): the checker and the CPU baseline only."""
+    if str(REPO / "oracle") not in sys.path:
+        sys.path.insert(0, str(REPO / "oracle"))
+    import ki_oracle
+
+    ki_oracle.build()
+    return ki_oracle
 
 
-def bench_copy(KI, D, steps, warmup, clocks):
+def oracle_sum_i64_window(o, seed: int, a: int, b: int) -> int:
+    """Wrapping Int64 sum of elements [a, b) of the U{-1000..1000} stream ``seed``, in chunks."""
+    tot, chunk = 0, 1 << 26
+    for c in range(a, b, chunk):
+        m = min(chunk, b - c)
+        tot = wrap64(tot + o.sum_i64(o.gen_int_range_i64(window_seed(seed, c), -1000, 1000, m)))
+    return tot
+
+
+# ---------------------------------------------------------------------------------------------
+# headline: sharded Int64 scan of 2^30 elements
+# ---------------------------------------------------------------------------------------------
+def bench_scan(KI, D, comm, steps, warmup, clocks):
     import torch
 
     dev = torch.device("cuda", D.dev)
-    src = torch.empty(COPY_BYTES + 16, dtype=torch.uint8, device=dev)
-    dst = torch.empty(COPY_BYTES + 16, dtype=torch.uint8, device=dev)
-    KI.fill_bytes(src, seed=2 + D.rank)
+    lo, hi = comm.scan_shard_range(SCAN_N)
+    n = hi - lo
+    x = torch.empty(n, dtype=torch.int64, device=dev)
+    KI.fill_int_range(x, seed=window_seed(3, lo), lo=-1000, hi=1000)  # this rank's window of the global input
+    y = torch.empty_like(x)
     stream = torch.cuda.current_stream(dev)
-
-    def step(ev=None):
-        for k, (so, do) in enumerate(PAIRS):
-            if ev is not None:
-                ev[k][0].record(stream)
-            KI.vcopy(dst, src, COPY_BYTES, dst_offset=do, src_offset=so)
-            if ev is not None:
-                ev[k][1].record(stream)
-
+    step = lambda: comm.scan(x, out=y)  # noqa: E731
     for _ in range(warmup):
         step()
-    # correctness spot check outside the timed region
-    KI.vcopy(dst, src, COPY_BYTES - 5, dst_offset=7, src_offset=3)
-    assert torch.equal(dst[7:7 + COPY_BYTES - 5], src[3:3 + COPY_BYTES - 5])
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in PAIRS]
-           for _ in range(steps)]
+    comm.check()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     D.barrier()
     t0 = time.time()
     start.record(stream)
-    for s in range(steps):
-        step(evs[s])
+    for a, b in evs:
+        a.record(stream)
+        step()
+        b.record(stream)
     end.record(stream)
     torch.cuda.synchronize()
     clocks.mark(t0, time.time())
+    comm.check()
     ms = D.max(start.elapsed_time(end))
-    kern_ms = [e[0].elapsed_time(e[1]) for st in evs for e in st]
-    launches = steps * len(PAIRS)
-    bytes_total = 2 * COPY_BYTES * launches * D.world
-    out = {"ms_total": ms, "ms_per_step": ms / steps, "value_gbs": bytes_total / (ms * 1e-3) / 1e9,
-           "kernel_ms_avg": statistics.mean(kern_ms), "kernel_ms_median": statistics.median(kern_ms),
-           "launches": launches, "bytes_per_launch": 2 * COPY_BYTES}
-    del src, dst
-    torch.cuda.empty_cache()
-    return out
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    if D.world == 1:
+        # one step is one launch of scan_i64_kernel (plus the clear of its tile status words)
+        kern_ms = statistics.mean(step_ms)
+        how = "CUDA events around each of the timed steps (one scan_i64_kernel launch per step)"
+    else:
+        # the step also holds phase 1 and the exchange: time the phase-2 kernel alone on this shard
+        ks = []
+        for _ in range(max(steps, 5)):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            KI.warpreduce_scan(x, out=y)
+            b.record(stream)
+            ks.append((a, b))
+        torch.cuda.synchronize()
+        kern_ms = D.max(statistics.mean(a.elapsed_time(b) for a, b in ks))
+        how = "CUDA events around launches of scan_i64_kernel alone on each rank's shard after the timed steps (max over ranks)"
+        step()  # leave y holding the sharded result for the parity check
+        torch.cuda.synchronize()
+        comm.check()
+    kernels_per_step = 1 if D.world == 1 else (2 if comm.rank == D.world - 1 else 3)
+    launches = sum(D.gather(kernels_per_step * steps))
+    parity = parity_scan(D, x, y, lo, hi)
+    out = {"ms_total": ms, "ms_per_step": ms / steps, "value_gbs": 16 * SCAN_N * steps / (ms * 1e-3) / 1e9,
+           "kernel_ms_avg": kern_ms, "kernel_timing": how, "launches": launches, "n_local": n, "lo": lo,
+           "step_ms_median": D.max(statistics.median(step_ms)), "parity": parity}
+    return out, x, y
 
 
-def bench_copy_e2e(KI, D, steps):
-    """Host buffers in pinned memory; every step is one ki_vcopy_host call: the source crosses to the
-    device, the copy kernel runs there and the result comes back, chunked so both directions overlap."""
+def parity_scan(D, x, y, lo, hi) -> dict:
+    """Checks of this rank's slice of cumsum(global input), outside the timed region:
+    (a) y[i] - y[i-1] == x[i] over the whole shard, on the device (chunks);
+    (b) y[0] - x[0] == the previous rank's last value (0 on rank 0): with (a) this fixes every value;
+    (c) the first and last 2^16 values against the oracle's cumsum of the regenerated global input,
+        seeded with the oracle's sum of everything before the window."""
+    import numpy as np
+    import torch
+
+    o = oracle_mod()
+    n = hi - lo
+    ok_diff = True
+    ch = 1 << 26
+    for a in range(1, n, ch):
+        b = min(n, a + ch)
+        ok_diff = ok_diff and bool(torch.equal(y[a:b] - y[a - 1:b - 1], x[a:b]))
+    first = wrap64(int(y[0].item()) - int(x[0].item()))
+    lasts = D.gather(int(y[-1].item()))
+    ok_edge = first == (0 if D.rank == 0 else lasts[D.rank - 1])
+    w = min(1 << 16, n)
+    prefix = oracle_sum_i64_window(o, 3, 0, lo)
+    xw = o.gen_int_range_i64(window_seed(3, lo), -1000, 1000, w)
+    ok_head = bool(np.array_equal(y[:w].cpu().numpy(), o.cumsum_i64(xw, seed=prefix)))
+    p2 = wrap64(prefix + oracle_sum_i64_window(o, 3, lo, hi - w))
+    xw2 = o.gen_int_range_i64(window_seed(3, hi - w), -1000, 1000, w)
+    ok_tail = bool(np.array_equal(y[n - w:].cpu().numpy(), o.cumsum_i64(xw2, seed=p2)))
+    ok = D.all_ok(ok_diff and ok_edge and ok_head and ok_tail)
+    return {"result": "ok" if ok else "MISMATCH", "checks": "difference property over every shard, shard boundaries, "
+            "first and last 2^16 values of every shard vs the oracle's cumsum (bit-exact)",
+            "rank0": {"diff": ok_diff, "boundary": ok_edge, "head": ok_head, "tail": ok_tail}}
+
+
+def bench_scan_e2e(KI, D, comm, x, y, steps):
+    """The same sharded scan through the host-buffer entry point: every step each rank's shard goes from
+    pinned host memory to the device and its scanned slice comes back (ki_scan_inclusive_i64_sharded_host;
+    with one rank the chunked pipeline of ki_scan_inclusive_i64_host, both copy directions overlapped)."""
     import torch
 
     dev = torch.device("cuda", D.dev)
-    n = COPY_BYTES
-    src_h = torch.empty(n + 16, dtype=torch.uint8, pin_memory=True)
-    dst_h = torch.empty(n + 16, dtype=torch.uint8, pin_memory=True)
-    tmp = torch.empty(n + 16, dtype=torch.uint8, device=dev)
-    KI.fill_bytes(tmp, seed=2 + D.rank)
-    src_h.copy_(tmp)
-    del tmp
+    n = x.numel()
+    xh = torch.empty(n, dtype=torch.int64, pin_memory=True)
+    yh = torch.empty(n, dtype=torch.int64, pin_memory=True)
+    xh.copy_(x)
     stream = torch.cuda.current_stream(dev)
-
-    def step(k):
-        so, do = PAIRS[(k * 37) % len(PAIRS)]
-        KI.vcopy_host(dst_h, src_h, n, dst_offset=do, src_offset=so, device=D.dev, stream=stream)
-
-    for k in range(2):
-        step(k)
+    comm.scan_host(xh, out=yh)
     torch.cuda.synchronize()
+    comm.check()
     D.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for k in range(steps):
-        step(k)
+    for _ in range(steps):
+        comm.scan_host(xh, out=yh)
     b.record(stream)
     torch.cuda.synchronize()
+    comm.check()
     ms = D.max(a.elapsed_time(b))
-    so, do = PAIRS[((steps - 1) * 37) % len(PAIRS)]
-    assert torch.equal(dst_h[do:do + n], src_h[so:so + n])
-    val = 2 * n * steps * D.world / (ms * 1e-3) / 1e9
-    del src_h, dst_h
-    torch.cuda.empty_cache()
-    return {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": n, "d2h_bytes_per_step": n,
-            "steps": steps, "ms_per_step": ms / steps,
-            "path": "ki_vcopy_host: pinned host buffers, 16 MiB chunks over 3 streams (H2D, kernel, D2H overlapped)"}
+    ok = True
+    ch = 1 << 26
+    for s0 in range(0, n, ch):
+        s1 = min(n, s0 + ch)
+        ok = ok and bool(torch.equal(yh[s0:s1], y[s0:s1].cpu()))
+    ok = D.all_ok(ok)
+    val = 16 * SCAN_N * steps / (ms * 1e-3) / 1e9
+    path = ("ki_scan_inclusive_i64_host: 16 MiB chunks over 3 streams (H2D, scan, D2H overlapped)" if D.world == 1 else
+            "ki_scan_inclusive_i64_sharded_host: shard to the device in 16 MiB chunks (each summed as it lands), "
+            "totals exchanged, chunks scanned in place and sent back as they finish")
+    del xh, yh
+    return {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": 8 * SCAN_N, "d2h_bytes_per_step": 8 * SCAN_N,
+            "steps": steps, "ms_per_step": round(ms / steps, 3), "path": path,
+            "parity": "ok (equal to the device-resident result)" if ok else "MISMATCH"}
 
 
 # ---------------------------------------------------------------------------------------------
 # the other primitives
 # ---------------------------------------------------------------------------------------------
+PAIRS = [(so, do) for do in range(16) for so in range(16)]
+
+
 def _timed_steps(D, stream, step, steps, warmup, between=None):
-    """Per-step device times (events around each step only) -> max over ranks of the mean."""
+    """Per-step device times (events around each step only) -> max over ranks of the mean and median."""
     import torch
 
     for _ in range(warmup):
@@ -410,91 +499,120 @@ def _timed_steps(D, stream, step, steps, warmup, between=None):
     return D.max(statistics.mean(ms)), D.max(statistics.median(ms))
 
 
-def bench_reduce(KI, D, steps, warmup, hbm):
+def bench_copy(KI, D, steps, warmup, hbm, src_kind):
+    """copyto! of 2^28 bytes: one step = 256 copies, one per (src_offset, dst_offset) in 0..15^2."""
     import torch
 
-    from kernelintrinsics import sharded
+    dev = torch.device("cuda", D.dev)
+    src = torch.empty(COPY_BYTES + 16, dtype=torch.uint8, device=dev)
+    dst = torch.empty(COPY_BYTES + 16, dtype=torch.uint8, device=dev)
+    KI.fill_bytes(src, seed=2 + D.rank)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        for k, (so, do) in enumerate(PAIRS):
+            if ev is not None:
+                ev[k][0].record(stream)
+            KI.vcopy(dst, src, COPY_BYTES, dst_offset=do, src_offset=so)
+            if ev is not None:
+                ev[k][1].record(stream)
+
+    for _ in range(warmup):
+        step()
+    KI.vcopy(dst, src, COPY_BYTES - 5, dst_offset=7, src_offset=3)
+    ok = D.all_ok(bool(torch.equal(dst[7:7 + COPY_BYTES - 5], src[3:3 + COPY_BYTES - 5])))
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in PAIRS]
+           for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    D.barrier()
+    start.record(stream)
+    for s in range(steps):
+        step(evs[s])
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = D.max(start.elapsed_time(end))
+    kern = statistics.mean(e[0].elapsed_time(e[1]) for st in evs for e in st)
+    bytes_total = 2 * COPY_BYTES * steps * len(PAIRS) * D.world
+    del src, dst
+    torch.cuda.empty_cache()
+    achieved = 2 * COPY_BYTES / (kern * 1e-3) / 1e9
+    return {"workload": "copyto! of 2^28 bytes, one step = 256 copies at (src_offset, dst_offset) in 0..15^2, "
+                        "each rank its own buffers (weak scaling)",
+            "value": round(bytes_total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms / steps, 4),
+            "kernel_ms_avg": round(kern, 5), "frac_of_hbm_per_gpu": round(achieved / hbm, 4),
+            "roofline": roofline("hbm", achieved, hbm, "GB/s", int(NCU_TRAFFIC_PER_ELEM["vcopy_kernel"] * COPY_BYTES),
+                                 src_kind),
+            "launches": steps * len(PAIRS) * D.world, "parity": "ok" if ok else "MISMATCH",
+            "l2": "inputs larger than L2 (256 MiB source + 256 MiB destination)"}
+
+
+def bench_reduce(KI, D, comm, steps, warmup, hbm):
+    """Float32 sum of 2^24 elements in total, sharded; steps replayed from one CUDA graph (a ~12 us
+    operation is shorter than a launch through Python).  The graph starts right after one sharded
+    reduce, whose exchange lines the ranks up, so the timed replays start together."""
+    import numpy as np
+    import torch
 
     dev = torch.device("cuda", D.dev)
-    lo, hi = sharded.shard_range(REDUCE_N, D.world, D.rank)
-    # 8 rotating inputs (8 x 64 MiB at N=1, more than L2): each step reads data that is not in L2.
-    nbuf = max(8, (1 << 29) // max(4 * (hi - lo), 1))
-    xs = [torch.empty(hi - lo, dtype=torch.float32, device=dev) for _ in range(nbuf)]
+    lo, hi = comm.shard_range(REDUCE_N)
+    n = hi - lo
+    nbuf = max(8, (1 << 29) // max(4 * n, 1))  # more bytes than L2 in the rotation
+    xs = [torch.empty(n, dtype=torch.float32, device=dev) for _ in range(nbuf)]
     for k, x in enumerate(xs):
-        KI.fill_uniform(x, seed=1 + k)  # shard-local streams; the parity tests check the global one
+        KI.fill_uniform(x, seed=window_seed(11 + k, lo))
     stream = torch.cuda.current_stream(dev)
     out = torch.empty((), dtype=torch.float64, device=dev)
     it = [0]
 
     def step():
-        x = xs[it[0] % nbuf]
+        comm.reduce_sum(xs[it[0] % nbuf], out_f64=out)
         it[0] += 1
-        if D.world == 1:
-            KI.warpfold_reduce(x, out_f64=out)
-        else:
-            sharded.reduce_sharded(x)
 
-    if D.world == 1:
-        # A ~12 us kernel is shorter than one host launch through Python: replay the steps from a
-        # CUDA graph so the device time is measured, not the launch path.
-        for _ in range(warmup):
-            step()
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        cs = torch.cuda.Stream(dev)
-        with torch.cuda.stream(cs):
-            with torch.cuda.graph(g, stream=cs):
-                for _ in range(steps):
-                    step()
-        g.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        g.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-        mean_ms = med_ms = a.elapsed_time(b) / steps
-        how = f"one CUDA graph of {steps} back-to-back launches"
-        del g
-    else:
-        mean_ms, med_ms = _timed_steps(D, stream, step, steps, warmup)
-        how = "per-step events (reduce + NCCL all-gather)"
-    gbs = 4 * REDUCE_N / (mean_ms * 1e-3) / 1e9
-    per_gpu = gbs / D.world
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(g, stream=cs):
+            for _ in range(steps):
+                step()
+    D.barrier()
+    step()
+    g.replay()
+    torch.cuda.synchronize()
+    D.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step()  # lines the ranks up on the device
+    a.record(stream)
+    g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    comm.check()
+    ms = D.max(a.elapsed_time(b) / steps)
+    del g
+    # parity: the global 2^24 input of stream 1 (each rank its window) against the oracle's Float64 sum
+    x = xs[0]
+    KI.fill_uniform(x, seed=window_seed(1, lo))
+    tot = comm.reduce_sum(x).item()
+    comm.check()
+    o = oracle_mod()
+    ref = o.sum_f32(o.gen_uniform_f32(1, REDUCE_N))
+    same = len(set(D.gather(float(tot)))) == 1
+    ok = D.all_ok(same and abs(tot - ref) <= 1e-5 * math.log2(REDUCE_N) * abs(ref))
+    gbs = 4 * REDUCE_N / (ms * 1e-3) / 1e9
+    res = {"workload": f"Float32 sum n=2^24 in total, {D.world} shard(s), partials exchanged over NVLink",
+           "value": round(gbs, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
+           "frac_of_hbm_per_gpu": round(gbs / D.world / hbm, 4),
+           "timing": f"one CUDA graph of {steps} back-to-back sharded reduces"
+                     + (" (reduce + exchange kernel)" if D.world > 1 else " (one reduce_kernel launch each)"),
+           "l2": f"{nbuf} rotating inputs ({nbuf * 4 * n >> 20} MiB per rank > L2): no step reads cached data",
+           "algorithmic_bytes": 4 * REDUCE_N, "launches": steps * (2 if D.world > 1 else 1) * D.world,
+           "parity": {"result": "ok" if ok else "MISMATCH", "rel_err": abs(tot - ref) / abs(ref),
+                      "tolerance": 1e-5 * math.log2(REDUCE_N), "same_bits_on_every_rank": same}}
     del xs
     torch.cuda.empty_cache()
-    return {"workload": f"Float32 sum n=2^24 ({D.world} shard(s))", "value": round(gbs, 2), "unit": "GB/s",
-            "ms_per_step": round(mean_ms, 5), "ms_median": round(med_ms, 5),
-            "frac_of_hbm_per_gpu": round(per_gpu / hbm, 4), "timing": how,
-            "l2": f"{nbuf} rotating inputs ({nbuf * 4 * (hi - lo) >> 20} MiB > L2): no step reads cached data",
-            "algorithmic_bytes": 4 * REDUCE_N}
-
-
-def bench_scan(KI, D, steps, warmup, hbm):
-    import torch
-
-    from kernelintrinsics import sharded
-
-    dev = torch.device("cuda", D.dev)
-    lo, hi = sharded.shard_range(SCAN_N, D.world, D.rank)
-    x = torch.empty(hi - lo, dtype=torch.int64, device=dev)
-    KI.fill_int_range(x, seed=3 + D.rank, lo=-1000, hi=1000)
-    y = torch.empty_like(x)
-    stream = torch.cuda.current_stream(dev)
-    if D.world == 1:
-        step = lambda: KI.warpreduce_scan(x, out=y)
-    else:
-        step = lambda: sharded.scan_sharded(x, y)
-    mean_ms, med_ms = _timed_steps(D, stream, step, steps, warmup)
-    KI.context(D.dev).check()
-    gbs = 16 * SCAN_N / (mean_ms * 1e-3) / 1e9
-    assert y[0].item() == x[0].item() or D.rank > 0
-    del x, y
-    torch.cuda.empty_cache()
-    return {"workload": f"Int64 inclusive scan n=2^30 ({D.world} shard(s))", "value": round(gbs, 2),
-            "unit": "GB/s", "elements_per_s": round(SCAN_N / (mean_ms * 1e-3), 1), "ms_per_step": round(mean_ms, 4),
-            "frac_of_hbm_per_gpu": round(gbs / D.world / hbm, 4), "algorithmic_bytes": 16 * SCAN_N,
-            "bytes_moved_per_elem": 16 if D.world == 1 else 24, "l2": "inputs larger than L2"}
+    return res
 
 
 def bench_scan_f32(KI, D, steps, warmup, hbm):
@@ -510,52 +628,60 @@ def bench_scan_f32(KI, D, steps, warmup, hbm):
     stream = torch.cuda.current_stream(dev)
     mean_ms, med_ms = _timed_steps(D, stream, lambda: KI.scan(x, "+", out=y), steps, warmup)
     KI.context(D.dev).check()
+    # property check: differences of the Float64-accumulated prefix are the inputs to Float32 rounding
+    d = (y[1:].double() - y[:-1].double() - x[1:].double()).abs().max().item()
+    ok = D.all_ok(d <= 2.0 ** -24 * 2 * float(y[-1].item()) and abs(y[0].item() - x[0].item()) == 0)
     gbs = 8 * n * D.world / (mean_ms * 1e-3) / 1e9
     del x, y
     torch.cuda.empty_cache()
     return {"workload": "Float32 inclusive scan (cumsum) n=2^28 per rank, Float64 accumulation", "value": round(gbs, 2),
             "unit": "GB/s", "ms_per_step": round(mean_ms, 4), "frac_of_hbm_per_gpu": round(gbs / D.world / hbm, 4),
-            "algorithmic_bytes": 8 * n, "replicas": D.world, "l2": "inputs larger than L2"}
+            "algorithmic_bytes": 8 * n, "replicas": D.world, "l2": "inputs larger than L2",
+            "parity": "ok" if ok else "MISMATCH"}
 
 
-def bench_compact(KI, D, steps, warmup, hbm):
+def bench_compact(KI, D, comm, steps, warmup, hbm):
+    """filter/findall of x > 0.5 over 2^28 N(0,1) Float32 in total, sharded: each rank compacts its
+    window of the global input with global 1-based indices; counts exchanged over NVLink."""
+    import numpy as np
     import torch
 
-    from kernelintrinsics import sharded
-
     dev = torch.device("cuda", D.dev)
-    lo, hi = sharded.shard_range(COMPACT_N, D.world, D.rank)
+    lo, hi = comm.shard_range(COMPACT_N)
     x = torch.empty(hi - lo, dtype=torch.float32, device=dev)
-    KI.fill_normal(x, seed=4 + D.rank)
+    KI.fill_normal(x, seed=window_seed(4, lo))  # lo is even: the Box-Muller pairs line up with the global stream
     vals = torch.empty_like(x)
     idx = torch.empty(x.numel(), dtype=torch.int32, device=dev)
     cnt = torch.zeros((), dtype=torch.uint64, device=dev)
+    off = torch.zeros((), dtype=torch.uint64, device=dev)
+    tot = torch.zeros((), dtype=torch.uint64, device=dev)
     stream = torch.cuda.current_stream(dev)
-    if D.world == 1:
-        step = lambda: KI.vote_compact(x, 0.5, out_vals=vals, out_idx=idx, count=cnt, trim=False)
-        k_total = None
-    else:
-        ops = sharded.cuda_ops()
-        ops.compact_gt = lambda xx, thr, base: KI.vote_compact(xx, thr, out_vals=vals, out_idx=idx, count=cnt,
-                                                               index_base=base, trim=False)
-        step = lambda: sharded.compact_sharded(x, 0.5, lo, ops=ops)
+    step = lambda: comm.compact_gt(x, 0.5, 1 + lo, vals, idx, cnt, off, tot)  # noqa: E731
     mean_ms, med_ms = _timed_steps(D, stream, step, steps, warmup)
-    KI.context(D.dev).check()
+    comm.check()
     k = int(cnt.item())
-    if D.world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([k], dtype=torch.int64, device=dev)
-        dist.all_reduce(t)
-        k = int(t.item())
-    alg = 4 * COMPACT_N + 8 * k
+    counts = D.gather(k)
+    total = sum(counts)
+    o = oracle_mod()
+    xs = x.cpu().numpy()
+    rv, ri = o.filter_gt_f32(xs, 0.5, index_base=1 + lo)
+    ok = (k == rv.size and np.array_equal(vals[:k].cpu().numpy().view(np.uint32), rv.view(np.uint32))
+          and np.array_equal(idx[:k].cpu().numpy(), ri) and int(off.item()) == sum(counts[:D.rank])
+          and int(tot.item()) == total)
+    ok = D.all_ok(ok)
+    alg = 4 * COMPACT_N + 8 * total
     gbs = alg / (mean_ms * 1e-3) / 1e9
-    del x, vals, idx
+    res = {"workload": f"filter/findall x>0.5, n=2^28 N(0,1) in total, {D.world} shard(s), counts exchanged over NVLink",
+           "value": round(gbs, 2), "unit": "GB/s", "kept": total, "kept_frac": round(total / COMPACT_N, 5),
+           "ms_per_step": round(mean_ms, 4), "frac_of_hbm_per_gpu": round(gbs / D.world / hbm, 4),
+           "algorithmic_bytes": alg, "l2": "inputs larger than L2",
+           "parity": {"result": "ok" if ok else "MISMATCH",
+                      "checks": "count, every kept value and 1-based global index of every shard vs the oracle's "
+                                "filter/findall; offsets = exclusive prefix of the counts; totals"}}
+    sample = xs[:1 << 26].copy()
+    del x, vals, idx, xs
     torch.cuda.empty_cache()
-    return {"workload": f"filter/findall x>0.5, n=2^28 N(0,1) ({D.world} shard(s))", "value": round(gbs, 2),
-            "unit": "GB/s", "kept": k, "kept_frac": round(k / COMPACT_N, 5), "ms_per_step": round(mean_ms, 4),
-            "frac_of_hbm_per_gpu": round(gbs / D.world / hbm, 4), "algorithmic_bytes": alg,
-            "l2": "inputs larger than L2"}
+    return res, sample
 
 
 def bench_gemm(KI, D, steps, warmup, bf16):
@@ -576,17 +702,28 @@ def bench_gemm(KI, D, steps, warmup, bf16):
         return {"workload": "fp8 e4m3 GEMM 8192^3", "unavailable": str(e)}
     mean_ms, med_ms = _timed_steps(D, stream, lambda: KI.fp8_gemm(A, B, C), steps, warmup)
     tflops = 2 * M * N * K / (mean_ms * 1e-3) / 1e12
-    # measured fp8 reference point on this GPU: torch._scaled_mm (cuBLASLt) on the same shape
     ref = None
-    try:
+    try:  # measured fp8 reference point on this GPU: torch._scaled_mm (cuBLASLt) on the same shape
         a8 = A.view(torch.float8_e4m3fn)
         b8 = B.view(torch.float8_e4m3fn).t().contiguous().t()
         one = torch.ones((), dtype=torch.float32, device=dev)
-        f = lambda: torch._scaled_mm(a8, b8, scale_a=one, scale_b=one, out_dtype=torch.float32)
+        f = lambda: torch._scaled_mm(a8, b8, scale_a=one, scale_b=one, out_dtype=torch.float32)  # noqa: E731
         r_ms, _ = _timed_steps(D, stream, f, steps, warmup)
         ref = 2 * M * N * K / (r_ms * 1e-3) / 1e12
     except Exception:  # noqa: BLE001 - the reference point is optional
         ref = None
+    # parity on sampled rows against the oracle's Float64 GEMM of the dequantised inputs
+    o = oracle_mod()
+    import numpy as np
+
+    rows = [0, 1, 4095, 8191]
+    Ah, Bh = A.cpu().numpy(), B.cpu().numpy()
+    Ch = C.cpu().numpy()
+    errs = []
+    for r in rows:
+        R = o.gemm_e4m3_rows(Ah, Bh, r, r + 1)
+        errs.append(float(np.linalg.norm(Ch[r:r + 1].astype(np.float64) - R) / np.linalg.norm(R)))
+    ok = D.all_ok(max(errs) <= 1e-3)
     del A, B, C
     torch.cuda.empty_cache()
     fp8_peak = 2 * bf16
@@ -594,72 +731,112 @@ def bench_gemm(KI, D, steps, warmup, bf16):
             "ms_per_step": round(mean_ms, 4), "frac_of_2x_bf16_measured": round(tflops / fp8_peak, 4),
             "frac_of_nominal_4500": round(tflops / 4500.0, 4),
             "cublaslt_fp8_same_shape_tflops": None if ref is None else round(ref, 1),
-            "replicas": D.world}
+            "replicas": D.world, "parity": {"result": "ok" if ok else "MISMATCH", "rows": rows,
+                                            "max_rel_frobenius": max(errs), "tolerance": 1e-3}}
 
 
 # ---------------------------------------------------------------------------------------------
-# CPU baseline and the reference arm
+# CPU baselines (the oracle on this host's cores, rank 0 at N = 1) and the reference arm
 # ---------------------------------------------------------------------------------------------
-def cpu_copy_baseline(seconds: float):
-    """The oracle's multithreaded byte copy (restatement of copyto!) on this host's cores."""
-    import numpy as np
-
-    sys.path.insert(0, str(REPO / "oracle"))
-    import ki_oracle
-
-    ki_oracle.build()
-    th = os.cpu_count() or 1
-    src = ki_oracle.gen_bytes(2, COPY_BYTES + 16, th)
-    dst = np.empty_like(src)
-    reps, moved = 0, 0
+def _loop(fn, seconds, max_reps=1000):
+    reps = 0
     t0 = time.perf_counter()
     while True:
-        so, do = PAIRS[(reps * 37) % len(PAIRS)]
-        n = COPY_BYTES
-        ki_oracle.lib().ko_copy_bytes(dst.ctypes.data + do, src.ctypes.data + so, n, th)
+        fn(reps)
         reps += 1
-        moved += 2 * n
         el = time.perf_counter() - t0
-        if el >= seconds or reps >= 1000:
-            break
-    assert np.array_equal(dst[do:do + n], src[so:so + n])
-    return {"value": round(moved / el / 1e9, 3), "unit": "GB/s", "cores": th, "kind": "port",
-            "sample": f"{reps} copies of 2^28 bytes at cycling (src,dst) offsets, {el:.1f} s"}, reps, el
+        if el >= seconds or reps >= max_reps:
+            return reps, el
+
+
+def cpu_scan_baseline(seconds):
+    """The oracle's multithreaded cumsum (two passes over per-thread blocks) on a 2^28-element sample."""
+    import numpy as np
+
+    o = oracle_mod()
+    th = os.cpu_count() or 1
+    n = 1 << 28
+    x = o.gen_int_range_i64(3, -1000, 1000, n, th)
+    y = np.empty_like(x)
+    reps, el = _loop(lambda k: o.lib().ko_cumsum_i64(x.ctypes.data, y.ctypes.data, n, 0, th), seconds)
+    return {"value": round(16 * n * reps / el / 1e9, 3), "unit": "GB/s", "cores": th, "kind": "port",
+            "sample": f"{reps} cumsums of 2^28 Int64 (16 B per element), {el:.1f} s"}
+
+
+def cpu_sum_baseline(seconds):
+    o = oracle_mod()
+    th = os.cpu_count() or 1
+    x = o.gen_uniform_f32(1, REDUCE_N, th)
+    reps, el = _loop(lambda k: o.sum_f32(x, th), seconds, 100000)
+    return {"value": round(4 * REDUCE_N * reps / el / 1e9, 3), "unit": "GB/s", "cores": th, "kind": "port",
+            "sample": f"{reps} Float64-accumulated sums of 2^24 Float32, {el:.1f} s"}
+
+
+def cpu_filter_baseline(sample, seconds):
+    o = oracle_mod()
+    th = os.cpu_count() or 1
+    kept = [0]
+
+    def f(k):
+        kept[0] = o.filter_gt_f32(sample, 0.5, nthreads=th)[0].size
+
+    reps, el = _loop(f, seconds)
+    alg = 4 * sample.size + 8 * kept[0]
+    return {"value": round(alg * reps / el / 1e9, 3), "unit": "GB/s", "cores": th, "kind": "port",
+            "sample": f"{reps} filter/findall passes (count, prefix, write) over 2^26 N(0,1) Float32, {el:.1f} s"}
+
+
+def cpu_copy_baseline(seconds):
+    import numpy as np
+
+    o = oracle_mod()
+    th = os.cpu_count() or 1
+    src = o.gen_bytes(2, COPY_BYTES + 16, th)
+    dst = np.empty_like(src)
+
+    def f(k):
+        so, do = PAIRS[(k * 37) % len(PAIRS)]
+        o.lib().ko_copy_bytes(dst.ctypes.data + do, src.ctypes.data + so, COPY_BYTES, th)
+
+    reps, el = _loop(f, seconds)
+    return {"value": round(2 * COPY_BYTES * reps / el / 1e9, 3), "unit": "GB/s", "cores": th, "kind": "port",
+            "sample": f"{reps} copies of 2^28 bytes at cycling (src,dst) offsets, {el:.1f} s"}
+
+
+def headline_config(world):
+    return {"workload": SCAN_WORKLOAD, "n": SCAN_N, "elements_per_step": SCAN_N, "parallelism": f"shard{world}",
+            "split": "ki_comm_scan_shard_range (ranks below the last: 2 shares; last rank: 3 shares)",
+            "l2": "inputs larger than L2 (8 GiB in + 8 GiB out in total; >= 1 GiB per rank at N = 8)"}
+
+
+METRIC = "Int64 inclusive scan (cumsum) throughput, algorithmic GB/s (16 B per element)"
 
 
 def run_reference(args, D):
+    """Base.cumsum semantics on the host cores: the oracle's multithreaded C cumsum of the whole 2^30-element
+    input per step (rank 0 only; the other ranks exit)."""
     if D.rank != 0:
         return 0
     import numpy as np
 
-    sys.path.insert(0, str(REPO / "oracle"))
-    import ki_oracle
-
-    ki_oracle.build()
+    o = oracle_mod()
     th = os.cpu_count() or 1
-    src = ki_oracle.gen_bytes(2, COPY_BYTES + 16, th)
-    dst = np.empty_like(src)
-    lib = ki_oracle.lib()
-
-    def step(k):
-        so, do = PAIRS[(k * 37) % len(PAIRS)]
-        lib.ko_copy_bytes(dst.ctypes.data + do, src.ctypes.data + so, COPY_BYTES, th)
-
-    for k in range(args.warmup):
-        step(k)
+    x = o.gen_int_range_i64(3, -1000, 1000, SCAN_N, th)
+    y = np.empty_like(x)
+    lib = o.lib()
+    for _ in range(args.warmup):
+        lib.ko_cumsum_i64(x.ctypes.data, y.ctypes.data, SCAN_N, 0, th)
     t0 = time.perf_counter()
-    for k in range(args.steps):
-        step(k)
+    for _ in range(args.steps):
+        lib.ko_cumsum_i64(x.ctypes.data, y.ctypes.data, SCAN_N, 0, th)
     el = time.perf_counter() - t0
-    val = 2 * COPY_BYTES * args.steps / el / 1e9
-    line = {"metric": "vectorised byte copy bandwidth (copyto!, 2^28 B, all 256 src/dst misalignments)",
-            "value": round(val, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (splitmix64 bytes, seed 2)",
-            "config": {"workload": "copyto! of 2^28 bytes at (src_offset, dst_offset) in 0..15 x 0..15",
-                       "bytes_per_copy": COPY_BYTES, "sample_per_step": "one 2^28-byte copy (cycling pairs)"},
+    val = 16 * SCAN_N * args.steps / el / 1e9
+    line = {"metric": METRIC, "value": round(val, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic (splitmix64 stream, seed 3, U{-1000..1000})", "config": headline_config(args.gpus),
             "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": th, "kind": "port",
-                             "sample": f"{args.steps} copies of 2^28 bytes, C oracle memcpy on {th} threads"},
+                             "sample": f"{args.steps} cumsums of the whole 2^30-element input, C oracle on {th} threads"},
             "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -679,55 +856,78 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     D.init()
     import kernelintrinsics as KI
+    from kernelintrinsics import sharded
 
     KI.context(D.dev)
-    hbm, bf16, bf16_sus, src = peaks()
+    comm = sharded.Comm.create([D.dev])[0] if D.world == 1 else sharded.Comm.from_process_group(device=D.dev)
+    hbm, bf16, bf16_sus, src_kind = peaks()
     clocks = Clocks(D.dev)
     clocks.start()
     try:
-        head = bench_copy(KI, D, args.steps, args.warmup, clocks)
-        kernels = {}
+        head, x, y = bench_scan(KI, D, comm, args.steps, args.warmup, clocks)
+        e2e = bench_scan_e2e(KI, D, comm, x, y, 3)
+        del x, y
+        torch.cuda.empty_cache()
+        kernels, sample = {}, None
         if not args.no_extra:
             only = set(filter(None, args.only.split(",")))
-            plan = [("reduce", lambda: bench_reduce(KI, D, 50, 5, hbm)),
-                    ("scan", lambda: bench_scan(KI, D, 10, 3, hbm)),
+            plan = [("copy", lambda: bench_copy(KI, D, args.steps, args.warmup, hbm, src_kind)),
+                    ("reduce", lambda: bench_reduce(KI, D, comm, 50, 5, hbm)),
                     ("scan_f32", lambda: bench_scan_f32(KI, D, 10, 3, hbm)),
-                    ("compact", lambda: bench_compact(KI, D, 20, 3, hbm)),
+                    ("compact", lambda: bench_compact(KI, D, comm, 20, 3, hbm)),
                     ("gemm", lambda: bench_gemm(KI, D, 20, 3, bf16))]
             for name, fn in plan:
                 if only and name not in only:
                     continue
                 t0 = time.time()
-                kernels[name] = fn()
+                r = fn()
+                if name == "compact":
+                    r, sample = r
+                kernels[name] = r
                 clocks.mark(t0, time.time())
-        e2e = bench_copy_e2e(KI, D, 6)
     finally:
         clk = clocks.stop()
     cpu = None
     if D.world == 1 and D.rank == 0 and not args.no_cpu_baseline:
-        cpu, _, _ = cpu_copy_baseline(args.cpu_seconds)
-    achieved = head["bytes_per_launch"] / (head["kernel_ms_avg"] * 1e-3) / 1e9
+        cpu = cpu_scan_baseline(args.cpu_seconds)
+        if "reduce" in kernels:
+            kernels["reduce"]["cpu_baseline"] = cpu_sum_baseline(3.0)
+        if "compact" in kernels and sample is not None:
+            kernels["compact"]["cpu_baseline"] = cpu_filter_baseline(sample, 3.0)
+        if "copy" in kernels:
+            kernels["copy"]["cpu_baseline"] = cpu_copy_baseline(3.0)
+    n_local = head["n_local"]
+    achieved = 16 * n_local / (head["kernel_ms_avg"] * 1e-3) / 1e9
+    parity = {"scan": head["parity"], "e2e_scan": e2e.pop("parity")}
+    for k, v in kernels.items():
+        if isinstance(v, dict) and "parity" in v:
+            parity[k] = v["parity"]
+    bad = [k for k, v in parity.items() if "ok" not in (v if isinstance(v, str) else v.get("result", ""))]
     line = {
-        "metric": "vectorised byte copy bandwidth (copyto!, 2^28 B, all 256 src/dst misalignments)",
+        "metric": METRIC,
         "value": round(head["value_gbs"], 2), "unit": "GB/s", "n_gpus": D.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(head["ms_per_step"], 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (splitmix64 bytes, seed 2+rank)",
-        "config": {"workload": "copyto! of 2^28 bytes, one step = 256 copies at (src_offset, dst_offset) in 0..15^2",
-                   "bytes_per_copy": COPY_BYTES, "copies_per_step": len(PAIRS), "parallelism": f"dp{D.world}",
-                   "l2": "inputs larger than L2 (256 MiB source + 256 MiB destination)"},
-        "roofline": roofline("hbm", achieved, hbm, "GB/s", NCU_TRAFFIC_PER_LAUNCH["vcopy_kernel"], src),
-        "kernel_ms_avg": round(head["kernel_ms_avg"], 5),
+        "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic (splitmix64 stream, seed 3, U{-1000..1000}; each rank generates its window of the global input)",
+        "config": headline_config(D.world),
+        "roofline": roofline("hbm", achieved, hbm, "GB/s", int(NCU_TRAFFIC_PER_ELEM["scan_i64_kernel"] * n_local),
+                             src_kind),
+        "kernel_ms_avg": round(head["kernel_ms_avg"], 5), "kernel_timing": head["kernel_timing"],
         "e2e": e2e,
         "gpu_launches": head["launches"],
         "clocks": clk,
+        "parity": {"result": "ok" if not bad else "MISMATCH: " + ",".join(bad), **parity},
         "kernels": kernels,
     }
+    line["roofline"]["kernel"] = "scan_i64_kernel"
+    line["roofline"]["elements_per_launch"] = n_local
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if D.rank == 0:
         print(json.dumps(line), flush=True)
+    comm.close()
     D.close()
-    return 0
+    return 0 if not bad else 3
 
 
 if __name__ == "__main__":

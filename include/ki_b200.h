@@ -250,6 +250,11 @@ typedef enum { KI_XCHG_AUTO = 0, KI_XCHG_PEER = 1, KI_XCHG_NCCL = 2 } ki_exchang
 /* Contiguous shard [*lo, *lo + *count) of rank `rank` of n elements: the first n % nranks ranks hold
  * one element more.  Host only. */
 int ki_comm_shard_range(size_t n, int nranks, int rank, size_t* lo, size_t* count);
+/* The split that gives every rank of ki_scan_inclusive_i64_sharded the same bytes to move: ranks
+ * below the last read their shard twice (phase 1 sum, phase 2 scan: 24 B per element) and the last
+ * rank once (its total is never needed: 16 B per element), so the last rank gets 3/2 of a share;
+ * boundaries at n*2r/(2*nranks + 1) rounded down to a multiple of 256 elements.  Host only. */
+int ki_comm_scan_shard_range(size_t n, int nranks, int rank, size_t* lo, size_t* count);
 /* One process (or host thread) per GPU: one rank calls ki_comm_get_id and hands the id to the others
  * (any host channel), then every rank calls ki_comm_init_rank with its own device (0-based) and rank.
  * NCCL (libnccl.so.2, loaded at run time) exchanges the ranks' buffer handles once; with
@@ -276,9 +281,10 @@ int ki_comm_get_ctx(ki_comm* comm, ki_ctx** ctx);
  * the partials are added in rank order, so every rank gets the same bits. */
 int ki_reduce_sum_f32_sharded(ki_comm* comm, const float* d_x, size_t n_local, float* d_out_f32, double* d_out_f64,
                               void* stream);
-/* cumsum of the concatenated Int64 shards: rank r writes its slice.  Phase 1 sums the shard
- * (ki_reduce_sum_i64), the totals are exchanged, phase 2 is ki_scan_inclusive_i64_dseed seeded on
- * the device with the sum of the lower ranks' totals. */
+/* cumsum of the concatenated Int64 shards (any contiguous split): rank r writes its slice.  Phase 1
+ * sums the shard (ki_reduce_sum_i64; skipped on the last rank, whose total nobody needs), the totals
+ * are exchanged, phase 2 is ki_scan_inclusive_i64_dseed seeded on the device with the sum of the
+ * lower ranks' totals.  With one rank it is ki_scan_inclusive_i64. */
 int ki_scan_inclusive_i64_sharded(ki_comm* comm, const int64_t* d_in, int64_t* d_out, size_t n_local, void* stream);
 /* ki_scan_inclusive_i64_sharded with this rank's shard in HOST memory (h_in, h_out, 8-byte aligned;
  * page-locked for asynchrony): phase 1 brings the shard to the device in 16 MiB chunks and sums each

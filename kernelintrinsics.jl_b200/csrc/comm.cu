@@ -348,6 +348,20 @@ int ki_comm_shard_range(size_t n, int nranks, int rank, size_t* lo, size_t* coun
     return KI_OK;
 }
 
+int ki_comm_scan_shard_range(size_t n, int nranks, int rank, size_t* lo, size_t* count) {
+    if (nranks <= 0 || rank < 0 || rank >= nranks || !lo || !count) return KI_ERR_ARG;
+    // weights 2, ..., 2, 3 (the last rank moves 16 B per element, the others 24): boundaries at
+    // n * 2r / (2 nranks + 1), rounded down to 256 elements so every shard starts 2 KiB aligned
+    auto edge = [&](int r) -> size_t {
+        if (r >= nranks) return n;
+        const unsigned __int128 e = (unsigned __int128)n * (unsigned)(2 * r) / (unsigned)(2 * nranks + 1);
+        return (size_t)e & ~(size_t)255;
+    };
+    *lo = edge(rank);
+    *count = edge(rank + 1) - *lo;
+    return KI_OK;
+}
+
 int ki_comm_get_id(ki_comm_id* id) {
     if (!id) return KI_ERR_ARG;
     static_assert(sizeof(ncclUniqueId) <= sizeof(ki_comm_id), "ki_comm_id holds an ncclUniqueId");
@@ -568,6 +582,7 @@ int ki_reduce_sum_f32_sharded(ki_comm* comm, const float* d_x, size_t n_local, f
                               void* stream) {
     KI_CHECK_COMM(comm);
     if (!d_out_f32 && !d_out_f64) return ki::set_error(comm->ctx, KI_ERR_ARG, "reduce: no output");
+    if (comm->nranks == 1) return ki_reduce_sum_f32(comm->ctx, d_x, n_local, d_out_f32, d_out_f64, stream);
     KI_GUARD(comm->ctx);
     cudaStream_t s = ki::as_stream(stream);
     double* part = reinterpret_cast<double*>(comm->words + W_LOCAL);
@@ -578,11 +593,17 @@ int ki_reduce_sum_f32_sharded(ki_comm* comm, const float* d_x, size_t n_local, f
 
 int ki_scan_inclusive_i64_sharded(ki_comm* comm, const int64_t* d_in, int64_t* d_out, size_t n_local, void* stream) {
     KI_CHECK_COMM(comm);
+    if (comm->nranks == 1) return ki_scan_inclusive_i64(comm->ctx, d_in, d_out, n_local, 0, stream);
     KI_GUARD(comm->ctx);
     cudaStream_t s = ki::as_stream(stream);
     int64_t* total = reinterpret_cast<int64_t*>(comm->words + W_LOCAL);
     int64_t* seed = reinterpret_cast<int64_t*>(comm->words + W_SEED);
-    int rc = ki_reduce_sum_i64(comm->ctx, d_in, n_local, total, stream);
+    int rc = KI_OK;
+    if (comm->rank == comm->nranks - 1) {  // nobody reads the last shard's total: publish 0 unread
+        KI_CUDA(comm->ctx, cudaMemsetAsync(total, 0, sizeof(int64_t), s));
+    } else {
+        rc = ki_reduce_sum_i64(comm->ctx, d_in, n_local, total, stream);
+    }
     if (rc) return rc;
     rc = exchange(comm, XF_PREFIX_I64, comm->words + W_LOCAL, nullptr, nullptr, comm->words + W_SEED, nullptr, s);
     if (rc) return rc;

@@ -66,6 +66,31 @@ struct Shape {
     static constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 32 * 16;  // 126976 B at 8 rows
 };
 
+// Widening scans of 1- and 2-byte elements (sums and products into 64 bits) give each lane 64 or
+// 128 bytes of output per row: stored straight from registers, every 16-byte warp store would touch
+// 32 lines.  Instead the results go through a per-warp 2 KiB shared-memory stage (16 or 32 lanes'
+// outputs per round, swizzled so that neither the writes nor the read-back conflict on banks) and
+// leave as 512 contiguous bytes per warp store.
+#ifndef KI_SCAN_ANY_STAGE
+#define KI_SCAN_ANY_STAGE 1
+#endif
+template <class T, class Op>
+struct Stage {
+    using R = typename ki::Traits<T, Op>::R;
+    static constexpr int kLaneBytes = (int)(16 / sizeof(T)) * (int)sizeof(R);  // output bytes per lane and row
+    static constexpr bool kOn = KI_SCAN_ANY_STAGE && sizeof(T) <= 2 && kLaneBytes >= 64;
+    static constexpr int kWarpBytes = 2048;
+    static constexpr int kChunks = kLaneBytes / 16;                       // 16-byte chunks per lane: 4 or 8
+    static constexpr int kLanes = kOn ? kWarpBytes / kLaneBytes : 32;     // lanes per round: 32 or 16
+    static constexpr int kRounds = 32 / kLanes;
+    static constexpr size_t kBytes = kOn ? (size_t)kWorkWarps * kWarpBytes : 0;
+    // chunk q of lane l of a round sits at l * kChunks + swz(q, l): 8 consecutive lanes writing the
+    // same q, or 8 consecutive chunks read back, fall on 8 different 16-byte bank groups
+    __device__ static __forceinline__ int swz(int q, int l) {
+        return kChunks == 8 ? (q ^ (l & 7)) : ((q + (l >> 1)) & 3);
+    }
+};
+
 // The input is rows x cols (rows = 1 for a plain scan): row r starts ld_in elements after row r-1
 // in the input and ld_out after it in the output, and every row is a segment of its own, cut into
 // tpr tiles; tile t is chunk t % tpr of row t / tpr.
@@ -252,6 +277,47 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 if (lane == 0) before = id;
                 A run = op(carry, before);
                 const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
+                if constexpr (Stage<T, Op>::kOn) {
+                    if (full && a.vec_out) {
+                        using St = Stage<T, Op>;
+                        constexpr int kPer = (int)(16 / sizeof(R));
+                        uint4* stg = reinterpret_cast<uint4*>(smem_raw + S::kTileBytes) + (size_t)w * (St::kWarpBytes / 16);
+                        R* orow = out + out_first + (size_t)(w * S::kSpan + S::kRow * j);
+#pragma unroll 1
+                        for (int rd = 0; rd < St::kRounds; ++rd) {
+                            if ((int)lane / St::kLanes == rd) {
+                                const int ll = (int)lane % St::kLanes;
+#pragma unroll
+                                for (int q = 0; q < St::kChunks; ++q) {
+                                    alignas(16) R r[kPer];
+#pragma unroll
+                                    for (int p = 0; p < kPer; ++p) {
+                                        const A x = Tr::lift(v[jj].get(q * kPer + p));
+                                        if (EXCL) {
+                                            r[p] = Tr::lower(run);
+                                            run = op(run, x);
+                                        } else {
+                                            run = op(run, x);
+                                            r[p] = Tr::lower(run);
+                                        }
+                                    }
+                                    stg[ll * St::kChunks + St::swz(q, ll)] = *reinterpret_cast<const uint4*>(r);
+                                }
+                            }
+                            __syncwarp();
+                            uint4* g = reinterpret_cast<uint4*>(orow + (size_t)rd * St::kLanes * kE);
+#pragma unroll
+                            for (int c = 0; c < St::kWarpBytes / 16 / 32; ++c) {
+                                const int gi = c * 32 + (int)lane;
+                                const int ls = gi / St::kChunks, q = gi % St::kChunks;
+                                __stcs(g + gi, stg[ls * St::kChunks + St::swz(q, ls)]);
+                            }
+                            __syncwarp();
+                        }
+                        carry = op(carry, __shfl_sync(0xffffffffu, inc, 31));
+                        continue;
+                    }
+                }
                 if (full && a.vec_out) {
                     constexpr int kPer = (int)(16 / sizeof(R));  // results per 16-byte store
                     constexpr int kStores = kE / kPer;
@@ -473,12 +539,12 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, const Sca
     if (grid > ntiles) grid = ntiles;
     if (excl) {
         KI_CUDA(ctx, cudaFuncSetAttribute(scan_any_kernel<T, Op, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)S::kTileBytes));
-        scan_any_kernel<T, Op, true><<<(unsigned)grid, kThreads, S::kTileBytes, s>>>(a);
+                                          (int)(S::kTileBytes + Stage<T, Op>::kBytes)));
+        scan_any_kernel<T, Op, true><<<(unsigned)grid, kThreads, S::kTileBytes + Stage<T, Op>::kBytes, s>>>(a);
     } else {
         KI_CUDA(ctx, cudaFuncSetAttribute(scan_any_kernel<T, Op, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)S::kTileBytes));
-        scan_any_kernel<T, Op, false><<<(unsigned)grid, kThreads, S::kTileBytes, s>>>(a);
+                                          (int)(S::kTileBytes + Stage<T, Op>::kBytes)));
+        scan_any_kernel<T, Op, false><<<(unsigned)grid, kThreads, S::kTileBytes + Stage<T, Op>::kBytes, s>>>(a);
     }
     return ki::check_launch(ctx, "scan_any_kernel launch");
 }

@@ -55,6 +55,7 @@ SIGNATURES = {
     "ki_scan_inclusive_i64_host": (_i32, [_vp, _vp, _vp, _sz, _i64, _vp]),
     "ki_scan_inclusive_i64_sharded_host": (_i32, [_vp, _vp, _vp, _sz, _vp]),
     "ki_comm_shard_range": (_i32, [_sz, _i32, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
+    "ki_comm_scan_shard_range": (_i32, [_sz, _i32, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "ki_comm_get_id": (_i32, [_vp]),
     "ki_comm_init_rank": (_i32, [_i32, _i32, _i32, _vp, _i32, ctypes.POINTER(_vp)]),
     "ki_comm_create": (_i32, [_i32, ctypes.POINTER(_i32), ctypes.POINTER(_vp)]),

@@ -39,6 +39,18 @@ def shard_range(n: int, world: int, rank: int) -> tuple:
     return lo, hi
 
 
+def scan_shard_range(n: int, world: int, rank: int) -> tuple:
+    """[lo, hi) of ``rank`` under ki_comm_scan_shard_range: weights 2, ..., 2, 3 (the last rank of the
+    sharded scan reads its shard once, the others twice), boundaries rounded down to 256 elements."""
+    if world <= 0 or not 0 <= rank < world or n < 0:
+        raise ValueError("bad shard arguments")
+
+    def edge(r):
+        return n if r >= world else (n * 2 * r // (2 * world + 1)) & ~255
+
+    return edge(rank), edge(rank + 1)
+
+
 def exclusive_prefix(values) -> list:
     out, run = [], 0
     for v in values:
@@ -288,6 +300,10 @@ class Comm:
 
     def shard_range(self, n: int) -> tuple:
         return shard_range(n, self.nranks, self.rank)
+
+    def scan_shard_range(self, n: int) -> tuple:
+        """[lo, hi) of this rank under the split that equalises the sharded scan's bytes per rank."""
+        return scan_shard_range(n, self.nranks, self.rank)
 
     # -- sharded operations ------------------------------------------------------------------
     def reduce_sum(self, x, out_f64=None, out_f32=None, stream=None):

@@ -173,6 +173,20 @@ def test_c_shard_range_matches_python():
                 assert lib.ki_comm_shard_range(n, world, r, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_OK
                 a, b = shard_range(n, world, r)
                 assert (lo.value, cnt.value) == (a, b - a)
+    from kernelintrinsics.sharded import scan_shard_range
+
+    for n in (0, 1, 255, 256 * 17 + 3, 2**30, 2**30 + 7):
+        for world in (1, 2, 3, 4, 8):
+            spans = [scan_shard_range(n, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            for (a, b), (c, d) in zip(spans, spans[1:]):
+                assert b == c and a <= b and a % 256 == 0
+            for r in range(world):
+                assert lib.ki_comm_scan_shard_range(n, world, r, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_OK
+                assert (lo.value, lo.value + cnt.value) == spans[r]
+            if n >= 2**30 and world > 1:  # the last rank holds 3/2 of the others' share
+                sizes = [b - a for a, b in spans]
+                assert abs(sizes[-1] / sizes[0] - 1.5) < 1e-3
     assert lib.ki_comm_shard_range(10, 0, 0, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_ERR_ARG
     assert lib.ki_comm_shard_range(10, 2, 2, ctypes.byref(lo), ctypes.byref(cnt)) == _abi.KI_ERR_ARG
 

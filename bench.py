@@ -54,10 +54,10 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the headline kernel,
-# scan_i64_kernel: 1,035,870,000 B captured by ncu at n = 2^26 (profiles/scan_i64_kernel_2e26.md),
+# scan_i64_kernel: 1,040,247,808 B captured by ncu at n = 2^26 (profiles/scan_i64_kernel_2e26.md),
 # scaled by the elements a launch processes (the traffic grows in proportion: one read of the input,
 # one write of the output, ~8 B of tile status per 15872 elements).
-NCU_TRAFFIC_PER_ELEM = {"scan_i64_kernel": 1_035_870_000 / (1 << 26), "vcopy_kernel": 486_999_808 / (1 << 28)}
+NCU_TRAFFIC_PER_ELEM = {"scan_i64_kernel": 1_040_247_808 / (1 << 26), "vcopy_kernel": 486_999_808 / (1 << 28)}
 
 SCAN_WORKLOAD = ("Int64 inclusive prefix sum (cumsum) of n=2^30 U{-1000..1000}, contiguous shards over the GPUs "
                  "(ki_comm_scan_shard_range), shard totals exchanged over NVLink")
@@ -442,6 +442,7 @@ def bench_scan_e2e(KI, D, comm, x, y, steps):
     yh = torch.empty(n, dtype=torch.int64, pin_memory=True)
     xh.copy_(x)
     stream = torch.cuda.current_stream(dev)
+    D.barrier()  # the ranks pinned their buffers at different speeds: line them up before the first exchange
     comm.scan_host(xh, out=yh)
     torch.cuda.synchronize()
     comm.check()
@@ -860,6 +861,7 @@ def main():
 
     KI.context(D.dev)
     comm = sharded.Comm.create([D.dev])[0] if D.world == 1 else sharded.Comm.from_process_group(device=D.dev)
+    comm.set_wait_timeout(10.0)  # exchange waits absorb host-side skew between ranks (allocation, parity work)
     hbm, bf16, bf16_sus, src_kind = peaks()
     clocks = Clocks(D.dev)
     clocks.start()

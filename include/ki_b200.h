@@ -203,9 +203,15 @@ int ki_scan_rows(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in
  * start-up.  Same result as ki_scan_inclusive_i64, but needs no context and calls no cudaMalloc,
  * cudaFree or allocating routine: its tile-status scratch is a static device array sized for
  * n <= KI_SCAN_NOALLOC_MAX_N (about 400 KiB, held by every GPU that loads the library until exit).
- * n beyond that returns KI_ERR_ARG.  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress, with that device current): make it before any stream capture.
- * Every call shares the array; calls that overlap on the GPU race.  Uses the current device. */
+ * n beyond that returns KI_ERR_ARG.  Uses the calling thread's current device and CUDA context.  The
+ * first call in each CUDA context (each device's primary context, a context re-created after
+ * cudaDeviceReset, any other context) runs a one-time set-up: cudaGetSymbolAddress of the array
+ * (which also loads the module under lazy loading), cudaDeviceGetAttribute (SM count) and
+ * cudaFuncSetAttribute (shared memory); make that first call before any stream capture.  Every call
+ * also runs cudaFree(NULL) (frees nothing; binds the primary context if none is current) and reads
+ * the current context's ID.  Every call shares the array, which keeps the last call's contents (each
+ * call clears its tile flags first); calls that overlap on the GPU race.  A bounded wait that runs
+ * out is not reported (use the context API where that matters). */
 #define KI_SCAN_NOALLOC_MAX_N (1ull << 28)
 int ki_scan_inclusive_i64_noalloc(const int64_t* d_in, int64_t* d_out, size_t n, int64_t seed, void* stream);
 

@@ -39,7 +39,10 @@
 // more than the re-reads).  L2 eviction-priority policies do not change it either (2^28, median of
 // 20): evict_normal on the tile load 0.468 ms (0.469 without), evict_first on it 0.480, evict_first
 // policy on the output stores 0.485, plain stores 0.474, evict_first policy on the second-pass loads
-// as well 0.52, no L2 prefetch 0.535.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %,
+// as well 0.52, no L2 prefetch 0.535; the Int64 scan's hints (evict-last tile load, streaming
+// re-read) 0.51, and with its shape (one CTA of 31 work warps, 124 KiB tiles) 0.49.  Tiles kept in
+// shared memory with each warp refilling its span of the buffer as soon as it is written (two 32 KiB
+// buffers, 3 CTAs per SM) 0.59 ms; 64 KiB x 1 CTA 0.92; 16 KiB x 4 CTAs 0.73; 48 KiB x 2 CTAs 0.63.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %,
 // warps 41 % active).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #pragma once
 

@@ -272,8 +272,10 @@ int ki_comm_scan_shard_range(size_t n, int nranks, int rank, size_t* lo, size_t*
 int ki_comm_get_id(ki_comm_id* id);
 int ki_comm_init_rank(int device, int nranks, int rank, const ki_comm_id* id, int exchange, ki_comm** out);
 /* One host thread driving ndev GPUs (devs: distinct 0-based devices, all peer-capable, else
- * KI_ERR_UNSUPPORTED): comms[i] is rank i on devs[i].  No NCCL.  Issue the operation for every rank
- * (each call only enqueues work) before waiting on any of them. */
+ * KI_ERR_UNSUPPORTED): comms[i] is rank i on devs[i].  No NCCL.  Issue each operation on every rank
+ * before the next operation (operation-major) and before waiting on any of them: a rank's first
+ * call of an operation allocates that operation's scratch, and a device allocation may wait for the
+ * GPU's pending work, which includes an exchange that only completes once every rank has issued it. */
 int ki_comm_create(int ndev, const int* devs, ki_comm** comms);
 /* Collective for communicators from ki_comm_init_rank (a bounded barrier, then unmap and free);
  * for ki_comm_create's, destroy every rank's communicator once all their work is complete. */

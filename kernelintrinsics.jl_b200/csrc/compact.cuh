@@ -42,7 +42,13 @@
 // as well 0.52, no L2 prefetch 0.535; the Int64 scan's hints (evict-last tile load, streaming
 // re-read) 0.51, and with its shape (one CTA of 31 work warps, 124 KiB tiles) 0.49.  Tiles kept in
 // shared memory with each warp refilling its span of the buffer as soon as it is written (two 32 KiB
-// buffers, 3 CTAs per SM) 0.59 ms; 64 KiB x 1 CTA 0.92; 16 KiB x 4 CTAs 0.73; 48 KiB x 2 CTAs 0.63.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %,
+// buffers, 3 CTAs per SM) 0.59 ms; 64 KiB x 1 CTA 0.92; 16 KiB x 4 CTAs 0.73; 48 KiB x 2 CTAs 0.63.
+// Tiles held in registers (one CTA of 31 work warps per SM, each thread keeping its 16 values of
+// tile k and of tile k-1, a 3-stage TMA ring of 62 KiB tiles, the lookbacks run by a look warp
+// decoupled through mbarriers): 0.61-0.63 ms, and 1.04 ms with 31 KiB tiles: without a second pass
+// the DRAM bytes are the algorithmic ones, but each CTA then waits for its tile's prefix, and the
+// lookback chain over the ~150 tiles in flight sets the pace.  Every variant was checked against
+// this kernel's output (small, partial, misaligned and 2^28 inputs) before timing.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %,
 // warps 41 % active).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #pragma once
 

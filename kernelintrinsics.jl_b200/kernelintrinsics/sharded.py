@@ -234,7 +234,9 @@ class Comm:
     @classmethod
     def create(cls, devices) -> list:
         """One process driving several GPUs (0-based device ids): one Comm per device, rank i on
-        devices[i].  Issue each operation on every rank before waiting on any of them."""
+        devices[i].  Issue each operation on every rank before the next operation and before waiting
+        on any of them (a first call may allocate scratch, which can wait for the GPU's pending
+        exchange)."""
         import ctypes
 
         from . import _abi

@@ -78,10 +78,19 @@ def test_sharded_ops_single_process(world, KI, oracle):
             per.append((xi[lo:hi].contiguous(), xf[slo:shi].contiguous(), xn[clo:chi].contiguous(), clo))
             torch.cuda.synchronize(dev)
         for _ in range(2):
-            outs = []
-            for c, (xi, xf, xn, clo) in zip(comms, per):  # enqueue every rank before waiting on any
+            # one host thread: each operation is issued on every rank before the next operation (a
+            # rank's call may allocate scratch, which can wait for that GPU's pending exchange)
+            sums, scans_d, comps = [], [], []
+            for c, (xi, xf, xn, clo) in zip(comms, per):
                 with torch.cuda.device(c.device):
-                    outs.append((c.reduce_sum(xf), c.scan(xi), c.compact_gt(xn, 0.5, index_base=1 + clo)))
+                    sums.append(c.reduce_sum(xf))
+            for c, (xi, xf, xn, clo) in zip(comms, per):
+                with torch.cuda.device(c.device):
+                    scans_d.append(c.scan(xi))
+            for c, (xi, xf, xn, clo) in zip(comms, per):
+                with torch.cuda.device(c.device):
+                    comps.append(c.compact_gt(xn, 0.5, index_base=1 + clo))
+            outs = list(zip(sums, scans_d, comps))
             for c in comms:
                 c.check()
             sums = [o[0].item() for o in outs]

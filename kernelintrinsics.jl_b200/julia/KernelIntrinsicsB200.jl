@@ -20,10 +20,11 @@ export get_warpsize, devices, deviceid, context, check_device,
        Up, Down, Xor, Idx, All, AnyLane, Uni, Ballot,
        shfl!, warpreduce!, warpfold!, vote!, vload, vstore!, access_roundtrip!,
        warpfold_reduce, reduce_ki, mapreduce_ki, reduce_rows_ki,
-       warpreduce_scan!, warpreduce_scan_noalloc!, accumulate_ki!, accumulate_rows_ki!,
+       warpreduce_scan!, warpreduce_scan_host!, warpreduce_scan_noalloc!, accumulate_ki!, accumulate_rows_ki!,
        vote_compact, filter_ki, count_ki,
        vcopy!, vcopy2d!, vcopy_strided!, fp8_gemm!,
-       Comm, comm_id, comms, sum_sharded, cumsum_sharded!, findall_sharded, shard_range, abort!
+       Comm, comm_id, comms, sum_sharded, cumsum_sharded!, cumsum_sharded_host!, findall_sharded, shard_range,
+       abort!
 
 const libki = normpath(joinpath(@__DIR__, "..", "lib", "libki_b200.so"))
 
@@ -217,6 +218,17 @@ end
 warpreduce_scan!(y::CuVector{Int64}, x::CuVector{Int64}; seed::Integer = 0) =
     (_call(c -> ccall((:ki_scan_inclusive_i64, libki), Cint, (Ptr{Cvoid}, CuPtr{Int64}, CuPtr{Int64}, Csize_t, Int64, Ptr{Cvoid}),
                       c, x, y, length(x), seed, _stream())); y)
+"""cumsum of a HOST Int64 array through the GPU (16 MiB chunks cross PCIe, are scanned on the device,
+each seeded there with the previous chunk's last value, and come back; both directions overlap).
+Pin the arrays (CUDA.Mem.pin) for the copies to be asynchronous; returns after synchronising."""
+function warpreduce_scan_host!(y::Vector{Int64}, x::Vector{Int64}; seed::Integer = 0)
+    length(y) == length(x) || throw(DimensionMismatch("warpreduce_scan_host!"))
+    GC.@preserve x y _call(c -> ccall((:ki_scan_inclusive_i64_host, libki), Cint,
+                                      (Ptr{Cvoid}, Ptr{Int64}, Ptr{Int64}, Csize_t, Int64, Ptr{Cvoid}),
+                                      c, pointer(x), pointer(y), length(x), seed, _stream()))
+    CUDA.synchronize()
+    return y
+end
 """The same scan without a context and without allocating (callers that may not allocate device
 memory); n <= 2^28, calls must not overlap on the GPU, first call per device before any capture."""
 function warpreduce_scan_noalloc!(y::CuVector{Int64}, x::CuVector{Int64}; seed::Integer = 0)
@@ -398,6 +410,15 @@ cumsum_sharded!(c::Comm, y::CuVector{Int64}, x::CuVector{Int64}) =
     (_ccheck(c, ccall((:ki_scan_inclusive_i64_sharded, libki), Cint,
                       (Ptr{Cvoid}, CuPtr{Int64}, CuPtr{Int64}, Csize_t, Ptr{Cvoid}),
                       c.handle, x, y, length(x), _stream())); y)
+"""cumsum_sharded! with this rank's shard in HOST memory (pinned for asynchrony)."""
+function cumsum_sharded_host!(c::Comm, y::Vector{Int64}, x::Vector{Int64})
+    length(y) == length(x) || throw(DimensionMismatch("cumsum_sharded_host!"))
+    GC.@preserve x y _ccheck(c, ccall((:ki_scan_inclusive_i64_sharded_host, libki), Cint,
+                                      (Ptr{Cvoid}, Ptr{Int64}, Ptr{Int64}, Csize_t, Ptr{Cvoid}),
+                                      c.handle, pointer(x), pointer(y), length(x), _stream()))
+    CUDA.synchronize()
+    return y
+end
 """filter(>(t)) / findall(>(t)) over the concatenated Float32 shards; `first` is the 1-based global
 index of this shard's first element.  Returns (vals, idx, offset, total): this rank's part belongs
 at offset+1:offset+length(vals) of the global result."""

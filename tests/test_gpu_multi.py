@@ -107,6 +107,42 @@ def test_sharded_ops_single_process(world, KI, oracle):
             c.close()
 
 
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_ops_with_empty_shards(world, KI, oracle):
+    """n smaller than the number of ranks: the ranks past n hold empty shards and still take part in
+    every exchange (zero partials, zero totals, zero counts); twice in a row."""
+    import torch
+
+    from kernelintrinsics import sharded
+
+    _need(world)
+    comms = sharded.Comm.create(list(range(world)))
+    try:
+        n = world - 1
+        xi_h = np.arange(1, n + 1, dtype=np.int64) * 1000
+        xf_h = np.full(n, 0.75, dtype=np.float32)
+        for _ in range(2):
+            parts = []
+            for c in comms:
+                lo, hi = c.shard_range(n)
+                dev = torch.device("cuda", c.device)
+                parts.append((torch.from_numpy(xi_h[lo:hi]).to(dev), torch.from_numpy(xf_h[lo:hi]).to(dev), lo))
+            sums = [c.reduce_sum(p[1]) for c, p in zip(comms, parts)]
+            scans = [c.scan(p[0]) for c, p in zip(comms, parts)]
+            comps = [c.compact_gt(p[1], 0.5, index_base=1 + p[2]) for c, p in zip(comms, parts)]
+            for c in comms:
+                c.check()
+            assert all(s.item() == 0.75 * n for s in sums)
+            got = np.concatenate([s.cpu().numpy() for s in scans])
+            assert np.array_equal(got, np.cumsum(xi_h))
+            idx = np.concatenate([cp[1][:int(cp[2].item())].cpu().numpy() for cp in comps])
+            assert np.array_equal(idx, np.arange(1, n + 1, dtype=np.int32))
+            assert all(int(cp[4].item()) == n for cp in comps)
+    finally:
+        for c in comms:
+            c.close()
+
+
 def _worker(rank, world, port, exchange, results):
     import datetime
     import sys

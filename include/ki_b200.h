@@ -198,9 +198,9 @@ int ki_scan_rows(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in
                  size_t ld_out, size_t rows, size_t cols, const void* h_init, void* stream);
 
 /* Allocation-free scan.  No counterpart in the reference.
- * For callers that cannot allocate device memory: code running while a CUDA graph is captured,
- * hosts whose device memory belongs to another allocator, loops that forbid allocation after
- * start-up.  Same result as ki_scan_inclusive_i64, but needs no context and calls no cudaMalloc,
+ * For callers that cannot allocate device memory: hosts whose device memory belongs to another
+ * allocator (a pool that must not be bypassed or grown), loops that forbid allocation after
+ * start-up, code that must not stall the device as cudaMalloc may.  Same result as ki_scan_inclusive_i64, but needs no context and calls no cudaMalloc,
  * cudaFree or allocating routine: its tile-status scratch is a static device array sized for
  * n <= KI_SCAN_NOALLOC_MAX_N (about 400 KiB, held by every GPU that loads the library until exit).
  * n beyond that returns KI_ERR_ARG.  Uses the calling thread's current device and CUDA context.  The
@@ -208,8 +208,8 @@ int ki_scan_rows(ki_ctx* ctx, int op, int dtype, int exclusive, const void* d_in
  * cudaDeviceReset, any other context) runs a one-time set-up: cudaGetSymbolAddress of the array
  * (which also loads the module under lazy loading), cudaDeviceGetAttribute (SM count) and
  * cudaFuncSetAttribute (shared memory); make that first call before any stream capture.  Every call
- * also runs cudaFree(NULL) (frees nothing; binds the primary context if none is current) and reads
- * the current context's ID.  Every call shares the array, which keeps the last call's contents (each
+ * reads the current context's ID (cudaSetDevice binds the primary context first if none is
+ * current).  Every call shares the array, which keeps the last call's contents (each
  * call clears its tile flags first); calls that overlap on the GPU race.  A bounded wait that runs
  * out is not reported (use the context API where that matters). */
 #define KI_SCAN_NOALLOC_MAX_N (1ull << 28)

@@ -344,9 +344,9 @@ extern "C" int ki_scan_inclusive_i64_host(ki_ctx* ctx, const int64_t* h_in, int6
 // ---------------------------------------------------------------------------------------------
 // Allocation-free variant.
 //
-// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is being captured, hosts
-// whose memory is owned by another allocator (a Julia or Python pool that must not be bypassed), or
-// real-time loops that forbid allocation after start-up.  ki_scan_inclusive_i64_noalloc runs the
+// Some callers cannot call cudaMalloc: hosts whose device memory is owned by another allocator (a
+// Julia or Python pool that must not be bypassed or grown behind its back), real-time loops that
+// forbid allocation after start-up, and code that must not stall the device, as cudaMalloc may.  ki_scan_inclusive_i64_noalloc runs the
 // same kernel as ki_scan_inclusive_i64 but takes its tile-status scratch from the file-scope array
 // below instead of a context, so it needs no context and allocates nothing.
 //
@@ -361,10 +361,10 @@ extern "C" int ki_scan_inclusive_i64_host(ki_ctx* ctx, const int64_t* h_in, int6
 // device, a non-primary context, a primary context re-created after cudaDeviceReset) repeats the
 // set-up.  The set-up runs, once per context: cudaGetSymbolAddress (which also loads the module
 // under lazy loading), cudaDeviceGetAttribute (SM count) and cudaFuncSetAttribute (dynamic shared
-// memory).  Every call also runs cudaFree(NULL) (frees nothing; makes the device's primary context
-// current if no context is), cuCtxGetCurrent and cuCtxGetId (reached through
-// cudaGetDriverEntryPointByVersion, so the library does not link libcuda).  Make the first call in
-// each context before any stream capture.
+// memory).  Every call also runs cuCtxGetCurrent and cuCtxGetId, reached through
+// cudaGetDriverEntryPointByVersion so the library does not link libcuda; when no context is current
+// it first runs cudaGetDevice and cudaSetDevice, which bind the device's primary context.  Make the
+// first call in each context before any stream capture.
 //
 // All calls share the array and it keeps the last call's contents: each call clears the ticket, the
 // status word and the tile status words (cudaMemsetAsync on the cached address) before its launch,
@@ -408,10 +408,14 @@ unsigned long long current_context_id() {
         g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
         g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
     }
-    if (cudaFree(nullptr) != cudaSuccess) return 0;  // frees nothing; binds the primary context if none is current
     void* c = nullptr;
     unsigned long long id = 0;
-    if (g_ctx_get_current(&c) != 0 || !c) return 0;
+    if (g_ctx_get_current(&c) != 0) return 0;
+    if (!c) {  // no context current yet: cudaSetDevice initialises and binds the device's primary context
+        int dev = -1;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return 0;
+        if (g_ctx_get_current(&c) != 0 || !c) return 0;
+    }
     if (g_ctx_get_id(c, &id) != 0) return 0;
     return id;
 }

@@ -1,8 +1,8 @@
 """GPU: the allocation-free scan entry point, called through the C ABI.
 
-ki_scan_inclusive_i64_noalloc exists for callers that cannot allocate device memory (code running
-while a CUDA graph is captured, hosts whose device memory belongs to another allocator, loops that
-forbid allocation after start-up).  It must give exactly Base.cumsum (the oracle) and what the
+ki_scan_inclusive_i64_noalloc exists for callers that cannot allocate device memory (hosts whose
+device memory belongs to another allocator, loops that forbid allocation after start-up, code that
+must not stall the device as cudaMalloc may).  It must give exactly Base.cumsum (the oracle) and what the
 context-based entry point gives, on consecutive calls that share its static scratch.  This file is
 collected last on purpose.
 """

@@ -17,17 +17,21 @@
 //            UInt32).  An element's rank inside its row is
 //                sum over c of popc(ballot_c & lanes_below) + (kept components before it in its lane)
 //            which keeps source order (lane-major, then component).  The row's kept values and
-//            indices go to a per-warp shared-memory run at their ranks (an element that is not kept
-//            goes to its lane's discard slot, so there are no branches) and leave as coalesced
-//            evict-first stores at tile prefix + warp prefix + row prefix.
+//            indices go to a per-warp shared-memory stage at their ranks, where slot s holds output
+//            element G + s with G a multiple of 32: every run of 32 that fills up leaves as one whole,
+//            aligned line per output (evict-first stores) and the rest moves to the front of the stage.
 // Between taking a ticket and publishing that tile's count a CTA only waits for its own load and
 // its own second pass, never for a lookback.  Tiles that are not 16-byte aligned are read with plain
 // loads; in the partial last tile, elements past the end are excluded explicitly.
 //
-// Measured at n = 2^28 (0.467 ms, 0.57 of the copy peak): without the stores the same kernel takes
-// 0.235 ms.  Writing the output streams evicts tiles that wait for their prefix, so most second-pass
-// reads come back from DRAM; the prefetch turns them into one asynchronous bulk read per tile
-// (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read (also
+// Measured at n = 2^28: 0.435 ms (0.61 of the copy peak).  Writing each row's run out on its own
+// (unaligned 4-byte stores, most lines written in two parts by two store instructions) took 0.471
+// ms; with whole aligned lines, plain stores in place of evict-first ones 0.443, an evict-last tile
+// load with evict-first second reads 0.474, no L2 prefetch 0.510, two CTAs of 16 warps over 8-row
+// spans 0.437, batches of 4 rows 0.437.  The figures below were taken with the per-row write-out:
+// without the stores the kernel takes 0.235 ms.  Writing the output streams evicts tiles that wait
+// for their prefix, so most second-pass reads come back from DRAM; the prefetch turns them into one
+// asynchronous bulk read per tile (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read (also
 // with the lines demoted to normal priority after the second read: 0.48 ms), evict-first second
 // reads (0.50), tiles kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-
 // element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
@@ -93,7 +97,7 @@ struct CShape {
     static constexpr int kRow = 32 * kE;                      // elements per row
     static constexpr int kSpan = kRows * kRow;                 // elements per work warp
     static constexpr int kTile = kWorkWarps * kSpan;           // elements per tile
-    static constexpr int kStageSlots = kRow + 32;              // a row's run + one discard slot per lane
+    static constexpr int kStageSlots = kRow + 32;              // up to 31 carried over + one row's run
     static constexpr size_t kStageBytes = (size_t)kWorkWarps * kStageSlots * (sizeof(T) + sizeof(int32_t));
     static constexpr size_t kSmemBytes = kTileBytes + kStageBytes;
     static_assert(kTile * sizeof(T) == kTileBytes, "tile layout");
@@ -242,10 +246,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
             const int count = (int)min((size_t)kTile, a.n - first);
             const bool full = count == kTile;
             const bool vec_in = a.tma_in;
-            // outputs of this warp start at one pointer; offsets from it fit 32 bits
+            // this warp's outputs start at element `at`; the stage is aligned to 32 elements below it
             const int64_t at = o.tile_excl + o.warp_excl[w];
-            T* vals = VALS ? static_cast<T*>(a.out_vals) + at : nullptr;
-            int32_t* idxs = IDX ? a.out_idx + at : nullptr;
             const int i_lane = w * S::kSpan + kE * (int)lane;  // element of (row 0, component 0)
             // output index of that element; unsigned, so indices past the last element wrap
             // harmlessly instead of overflowing (they are never stored)
@@ -253,7 +255,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
             T* sv = reinterpret_cast<T*>(smem_raw + kTileBytes) + (size_t)w * S::kStageSlots;
             int32_t* si = reinterpret_cast<int32_t*>(smem_raw + kTileBytes + (size_t)kWorkWarps * S::kStageSlots * sizeof(T)) +
                           (size_t)w * S::kStageSlots;
-            int pos = 0;
+            // slot s of the stage holds output element G + s (G a multiple of 32); slots below `lo` belong
+            // to the previous warp's run and are never stored
+            int L = (int)(at & 31);  // slots in use
+            int lo = L;
+            T* vbase = VALS ? static_cast<T*>(a.out_vals) + (at - L) : nullptr;
+            int32_t* ibase = IDX ? a.out_idx + (at - L) : nullptr;
             // FULL: a whole tile (no element past the end), the common case, without bounds checks
             auto rows_pass = [&](auto full_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
@@ -286,30 +293,58 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
                             row += __popc(b[e]);
                         }
                         const uint32_t ix = ix0 + (uint32_t)(S::kRow * (j0 + j));
-                        // the row's kept elements, in source order, as one run in this warp's stage
-                        // (an element that is not kept goes to the lane's discard slot: no branches) ...
-                        const int junk = S::kRow + (int)lane;
-                        int r = ahead;
+                        // the row's kept elements, in source order, after the ones carried over
+                        int r = L + ahead;
 #pragma unroll
                         for (int e = 0; e < kE; ++e) {
-                            const int at_e = p[e] ? r : junk;
-                            if (VALS) sv[at_e] = v[j].v[e];
-                            if (IDX) si[at_e] = (int32_t)(ix + (uint32_t)e);
+                            if (p[e]) {
+                                if (VALS) sv[r] = v[j].v[e];
+                                if (IDX) si[r] = (int32_t)(ix + (uint32_t)e);
+                            }
                             r += (int)p[e];
                         }
                         __syncwarp();
-                        // ... written out with consecutive lanes on consecutive addresses
-                        for (int q = (int)lane; q < row; q += 32) {
-                            if (VALS) __stcs(vals + pos + q, sv[q]);
-                            if (IDX) __stcs(idxs + pos + q, si[q]);
+                        const int total = L + row;
+                        const int full_runs = total >> 5;
+                        if (full_runs > 0) {
+                            // whole runs of 32 leave as aligned lines, consecutive lanes on consecutive addresses
+                            for (int c = 0; c < full_runs; ++c) {
+                                const int sl = 32 * c + (int)lane;
+                                if (sl >= lo) {
+                                    if (VALS) __stcs(vbase + sl, sv[sl]);
+                                    if (IDX) __stcs(ibase + sl, si[sl]);
+                                }
+                            }
+                            // the remainder (< 32) moves to the front
+                            const int rem = total - 32 * full_runs;
+                            T tv{};
+                            int32_t ti = 0;
+                            if ((int)lane < rem) {
+                                if (VALS) tv = sv[32 * full_runs + lane];
+                                if (IDX) ti = si[32 * full_runs + lane];
+                            }
+                            __syncwarp();
+                            if ((int)lane < rem) {
+                                if (VALS) sv[lane] = tv;
+                                if (IDX) si[lane] = ti;
+                            }
+                            if (VALS) vbase += 32 * full_runs;
+                            if (IDX) ibase += 32 * full_runs;
+                            lo = 0;
+                            L = rem;
+                            __syncwarp();
+                        } else {
+                            L = total;
                         }
-                        __syncwarp();
-                        pos += row;
                     }
                 }
             };
             if (full) rows_pass(std::true_type{});
             else rows_pass(std::false_type{});
+            if ((int)lane >= lo && (int)lane < L) {  // the last, partial run
+                if (VALS) __stcs(vbase + lane, sv[lane]);
+                if (IDX) __stcs(ibase + lane, si[lane]);
+            }
             if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);
         }
         __syncthreads();  // the next ticket is visible; slot cur ^ 1 is free

@@ -28,7 +28,13 @@
 // (unaligned 4-byte stores, most lines written in two parts by two store instructions) took 0.471
 // ms; with whole aligned lines, plain stores in place of evict-first ones 0.443, an evict-last tile
 // load with evict-first second reads 0.474, no L2 prefetch 0.510, two CTAs of 16 warps over 8-row
-// spans 0.437, batches of 4 rows 0.437.  The figures below were taken with the per-row write-out:
+// spans 0.437, batches of 4 rows 0.437, lookback windows of 64 / 128 tiles 0.439 / 0.454, runs
+// written by bulk copies from the stage (each row then waits for its copy to read the stage) 0.70.
+// Second-pass reads hit L2 only while at most about 96 KiB of tiles per SM are in flight (48 KiB
+// tiles x 2 CTAs of 16 warps, 32 KiB x 3 CTAs, 36 KiB x 3 CTAs of 12 warps), and each of those
+// shapes is slower (0.47-0.51 ms): fewer bytes or warps in flight cost more than the re-reads.
+// The lookback's waits cost about 5 % (0.414 ms with a made-up prefix and no lookback).  The
+// figures below were taken with the per-row write-out:
 // without the stores the kernel takes 0.235 ms.  Writing the output streams evicts tiles that wait
 // for their prefix, so most second-pass reads come back from DRAM; the prefetch turns them into one
 // asynchronous bulk read per tile (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read (also

@@ -30,6 +30,8 @@
 // load with evict-first second reads 0.474, no L2 prefetch 0.510, two CTAs of 16 warps over 8-row
 // spans 0.437, batches of 4 rows 0.437, lookback windows of 64 / 128 tiles 0.439 / 0.454, runs
 // written by bulk copies from the stage (each row then waits for its copy to read the stage) 0.70.
+// Without the barrier at the end of each iteration (the next ticket delivered through the tile
+// mbarrier, three pending-tile slots) 0.518 ms, and 0.438 with two CTAs of 16 warps.
 // Second-pass reads hit L2 only while at most about 96 KiB of tiles per SM are in flight (48 KiB
 // tiles x 2 CTAs of 16 warps, 32 KiB x 3 CTAs, 36 KiB x 3 CTAs of 12 warps), and each of those
 // shapes is slower (0.47-0.51 ms): fewer bytes or warps in flight cost more than the re-reads.

@@ -28,7 +28,10 @@ enum ki_region {
 
 // Host-buffer pipelines: slots of staging memory cycled over three streams (host -> device,
 // kernel, device -> host), KI_PIPE_CHUNK bytes per chunk.
-constexpr int KI_PIPE_SLOTS = 4;
+#ifndef KI_PIPE_SLOTS_N
+#define KI_PIPE_SLOTS_N 4
+#endif
+constexpr int KI_PIPE_SLOTS = KI_PIPE_SLOTS_N;
 #ifndef KI_PIPE_CHUNK
 #define KI_PIPE_CHUNK (16u << 20)
 #endif

@@ -346,9 +346,10 @@ extern "C" int ki_scan_inclusive_i64_host(ki_ctx* ctx, const int64_t* h_in, int6
 //
 // Some callers cannot call cudaMalloc: hosts whose device memory is owned by another allocator (a
 // Julia or Python pool that must not be bypassed or grown behind its back), real-time loops that
-// forbid allocation after start-up, and code that must not stall the device, as cudaMalloc may.  ki_scan_inclusive_i64_noalloc runs the
-// same kernel as ki_scan_inclusive_i64 but takes its tile-status scratch from the file-scope array
-// below instead of a context, so it needs no context and allocates nothing.
+// forbid allocation after start-up, and code that must not stall the device, as cudaMalloc may.
+// ki_scan_inclusive_i64_noalloc runs the same kernel as ki_scan_inclusive_i64 but takes its
+// tile-status scratch from the file-scope array below instead of a context, so it needs no context
+// and allocates nothing.
 //
 // The array is sized for KI_SCAN_NOALLOC_MAX_N elements (a 256-byte header plus three 8-byte words
 // per tile: 16,913 tiles of 15872 elements, about 397 KiB).  Every GPU that loads this library

@@ -39,7 +39,8 @@
 // figures below were taken with the per-row write-out:
 // without the stores the kernel takes 0.235 ms.  Writing the output streams evicts tiles that wait
 // for their prefix, so most second-pass reads come back from DRAM; the prefetch turns them into one
-// asynchronous bulk read per tile (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or evict-first hint on the first read (also
+// asynchronous bulk read per tile (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or
+// evict-first hint on the first read (also
 // with the lines demoted to normal priority after the second read: 0.48 ms), evict-first second
 // reads (0.50), tiles kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-
 // element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
@@ -60,8 +61,8 @@
 // decoupled through mbarriers): 0.61-0.63 ms, and 1.04 ms with 31 KiB tiles: without a second pass
 // the DRAM bytes are the algorithmic ones, but each CTA then waits for its tile's prefix, and the
 // lookback chain over the ~150 tiles in flight sets the pace.  Every variant was checked against
-// this kernel's output (small, partial, misaligned and 2^28 inputs) before timing.  The kernel is latency-bound (ncu: DRAM 57 %, issue 59 %,
-// warps 41 % active).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
+// this kernel's output (small, partial, misaligned and 2^28 inputs) before timing.  The kernel is
+// latency-bound (ncu at 2^26: DRAM 59 %, issue 52 %, warps 41 % active, stalls mostly at barriers).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #pragma once
 
 #include "ki/common.cuh"
@@ -96,6 +97,7 @@ constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 512;  // 64 KiB: 1638
 #define KI_COMPACT_BATCH 8
 #endif
 constexpr int kBatch = KI_COMPACT_BATCH;  // rows loaded at once in the second pass
+static_assert(kRows % kBatch == 0, "the second pass loads whole batches of rows");
 constexpr int kLookbackK = KI_COMPACT_LOOKBACK_K;  // lookback window of 32*K tiles per round trip
 constexpr int kCtasPerSm = KI_COMPACT_CTAS_PER_SM;
 

@@ -40,6 +40,10 @@
 #include "ki/common.cuh"
 #include "ki/intrinsics.cuh"
 
+// Prepares a scan of up to n elements (scratch, kernel attributes) so that it can be enqueued later
+// without a blocking call (scan.cu).
+__attribute__((visibility("hidden"))) int ki_scan_i64_reserve(ki_ctx* ctx, size_t n);
+
 namespace {
 
 constexpr int kMaxRanks = KI_COMM_MAX_RANKS;
@@ -598,7 +602,9 @@ int ki_scan_inclusive_i64_sharded(ki_comm* comm, const int64_t* d_in, int64_t* d
     cudaStream_t s = ki::as_stream(stream);
     int64_t* total = reinterpret_cast<int64_t*>(comm->words + W_LOCAL);
     int64_t* seed = reinterpret_cast<int64_t*>(comm->words + W_SEED);
-    int rc = KI_OK;
+    // nothing after the exchange may block: phase 2's scratch and kernel are made ready first
+    int rc = ki_scan_i64_reserve(comm->ctx, n_local);
+    if (rc) return rc;
     if (comm->rank == comm->nranks - 1) {  // nobody reads the last shard's total: publish 0 unread
         KI_CUDA(comm->ctx, cudaMemsetAsync(total, 0, sizeof(int64_t), s));
     } else {
@@ -627,6 +633,7 @@ int ki_scan_inclusive_i64_sharded_host(ki_comm* comm, const int64_t* h_in, int64
     void* parts = nullptr;
     rc = ki::ensure_region(ctx, KI_REG_HOST_SHARD, n_local * sizeof(int64_t), &shard);
     if (!rc) rc = ki::ensure_region(ctx, KI_REG_HOST_PART, (nch + 1) * sizeof(int64_t), &parts);
+    if (!rc) rc = ki_scan_i64_reserve(ctx, kChunk);  // phase 2 (after the exchange) must not block
     if (rc) return rc;
     int64_t* buf = static_cast<int64_t*>(shard);
     int64_t* part = static_cast<int64_t*>(parts);

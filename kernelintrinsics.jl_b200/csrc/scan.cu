@@ -277,6 +277,20 @@ extern "C" int ki_scan_inclusive_i64(ki_ctx* ctx, const int64_t* d_in, int64_t* 
     return scan_i64_ctx(ctx, d_in, d_out, n, seed, nullptr, ki::as_stream(stream));
 }
 
+// Everything a scan of up to n elements needs before it can be enqueued without a blocking call:
+// the tile-status scratch (cudaMalloc on first use or growth) and the kernel's shared-memory
+// attribute (which also loads the kernel under lazy module loading).  Sharded scans call this before
+// their exchange: a cudaMalloc or a module load issued after it could wait for a device whose
+// exchange kernel waits for a rank that the same host thread has not reached yet.
+__attribute__((visibility("hidden"))) int ki_scan_i64_reserve(ki_ctx* ctx, size_t n) {
+    const size_t ntiles = (n + kTile - 1) / kTile;
+    void* base = nullptr;
+    int rc = ki::ensure_region(ctx, KI_REG_SCAN, 256 + ntiles * 24, &base);
+    if (rc) return rc;
+    KI_CUDA(ctx, cudaFuncSetAttribute(scan_i64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    return KI_OK;
+}
+
 extern "C" int ki_scan_inclusive_i64_dseed(ki_ctx* ctx, const int64_t* d_in, int64_t* d_out, size_t n,
                                            const int64_t* d_seed, void* stream) {
     KI_CHECK_CTX(ctx);

@@ -24,9 +24,13 @@
 // its own second pass, never for a lookback.  Tiles that are not 16-byte aligned are read with plain
 // loads; in the partial last tile, elements past the end are excluded explicitly.
 //
-// Measured at n = 2^28: 0.435 ms (0.61 of the copy peak).  Writing each row's run out on its own
-// (unaligned 4-byte stores, most lines written in two parts by two store instructions) took 0.471
-// ms; with whole aligned lines, plain stores in place of evict-first ones 0.443, an evict-last tile
+// Measured at n = 2^28: 0.427 ms (0.62 of the copy peak), with Float32 / 4-byte values staged as
+// one 8-byte {value, index} slot per element, the row's count taken from lane 31's rank by one
+// shuffle (not four popc) and second-pass batches of 4 rows (0.435 ms with two 4-byte stage arrays,
+// four popc and batches of 8; packed slots with batches of 8 spill: 0.443).  Writing each row's run
+// out on its own (unaligned 4-byte stores, most lines written in two parts by two store
+// instructions) took 0.471 ms; with whole aligned lines (and the two stage arrays), plain stores in
+// place of evict-first ones 0.443, an evict-last tile
 // load with evict-first second reads 0.474, no L2 prefetch 0.510, two CTAs of 16 warps over 8-row
 // spans 0.437, batches of 4 rows 0.437, lookback windows of 64 / 128 tiles 0.439 / 0.454, runs
 // written by bulk copies from the stage (each row then waits for its copy to read the stage) 0.70.
@@ -94,7 +98,7 @@ constexpr int kThreads = kWorkThreads + 32;
 constexpr int kRows = KI_COMPACT_ROWS;  // rows of 32 lanes x one 16-byte vector per work warp
 constexpr size_t kTileBytes = (size_t)kWorkWarps * kRows * 512;  // 64 KiB: 16384 elements of 4 bytes or 8192 of 8
 #ifndef KI_COMPACT_BATCH
-#define KI_COMPACT_BATCH 8
+#define KI_COMPACT_BATCH 4
 #endif
 constexpr int kBatch = KI_COMPACT_BATCH;  // rows loaded at once in the second pass
 static_assert(kRows % kBatch == 0, "the second pass loads whole batches of rows");
@@ -120,6 +124,14 @@ struct PLt { template <class T> __device__ static __forceinline__ bool test(T x,
 struct PLe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x <= t; } };
 struct PEq { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x == t; } };
 struct PNe { template <class T> __device__ static __forceinline__ bool test(T x, T t) { return x != t; } };
+
+template <class T>
+__device__ __forceinline__ uint32_t bits32(T v) {
+    static_assert(sizeof(T) == 4, "4-byte values");
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    return u;
+}
 
 struct CompactArgs {
     const void* x;
@@ -265,6 +277,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
             T* sv = reinterpret_cast<T*>(smem_raw + kTileBytes) + (size_t)w * S::kStageSlots;
             int32_t* si = reinterpret_cast<int32_t*>(smem_raw + kTileBytes + (size_t)kWorkWarps * S::kStageSlots * sizeof(T)) +
                           (size_t)w * S::kStageSlots;
+            // 4-byte elements with both outputs: one 8-byte {value bits, index} slot per element (one
+            // shared store and load per element instead of two)
+            constexpr bool kPack = sizeof(T) == 4 && VALS && IDX;
+            uint2* sp = reinterpret_cast<uint2*>(smem_raw + kTileBytes) + (size_t)w * S::kStageSlots;
             // slot s of the stage holds output element G + s (G a multiple of 32); slots below `lo` belong
             // to the previous warp's run and are never stored
             int L = (int)(at & 31);  // slots in use
@@ -293,14 +309,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
                         const int i0 = i_lane + S::kRow * (j0 + j);
                         bool p[kE];
                         unsigned b[kE];
-                        int ahead = 0, row = 0;
+                        int ahead = 0;
 #pragma unroll
                         for (int e = 0; e < kE; ++e) {
                             p[e] = P::test(v[j].v[e], thr);
                             if (!FULL) p[e] = p[e] && (i0 + e < count);
                             b[e] = ki::ballot(p[e]);
                             ahead += __popc(b[e] & below);
-                            row += __popc(b[e]);
                         }
                         const uint32_t ix = ix0 + (uint32_t)(S::kRow * (j0 + j));
                         // the row's kept elements, in source order, after the ones carried over
@@ -308,11 +323,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
 #pragma unroll
                         for (int e = 0; e < kE; ++e) {
                             if (p[e]) {
-                                if (VALS) sv[r] = v[j].v[e];
-                                if (IDX) si[r] = (int32_t)(ix + (uint32_t)e);
+                                if constexpr (kPack) {
+                                    sp[r] = make_uint2(bits32(v[j].v[e]), ix + (uint32_t)e);
+                                } else {
+                                    if (VALS) sv[r] = v[j].v[e];
+                                    if (IDX) si[r] = (int32_t)(ix + (uint32_t)e);
+                                }
                             }
                             r += (int)p[e];
                         }
+                        const int row = __shfl_sync(0xffffffffu, r, 31) - L;  // kept in this row
                         __syncwarp();
                         const int total = L + row;
                         const int full_runs = total >> 5;
@@ -321,22 +341,35 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
                             for (int c = 0; c < full_runs; ++c) {
                                 const int sl = 32 * c + (int)lane;
                                 if (sl >= lo) {
-                                    if (VALS) __stcs(vbase + sl, sv[sl]);
-                                    if (IDX) __stcs(ibase + sl, si[sl]);
+                                    if constexpr (kPack) {
+                                        const uint2 q = sp[sl];
+                                        __stcs(vbase + sl, ki::from_bits<T>(q.x));
+                                        __stcs(ibase + sl, (int32_t)q.y);
+                                    } else {
+                                        if (VALS) __stcs(vbase + sl, sv[sl]);
+                                        if (IDX) __stcs(ibase + sl, si[sl]);
+                                    }
                                 }
                             }
                             // the remainder (< 32) moves to the front
                             const int rem = total - 32 * full_runs;
-                            T tv{};
-                            int32_t ti = 0;
-                            if ((int)lane < rem) {
-                                if (VALS) tv = sv[32 * full_runs + lane];
-                                if (IDX) ti = si[32 * full_runs + lane];
-                            }
-                            __syncwarp();
-                            if ((int)lane < rem) {
-                                if (VALS) sv[lane] = tv;
-                                if (IDX) si[lane] = ti;
+                            if constexpr (kPack) {
+                                uint2 tq = make_uint2(0u, 0u);
+                                if ((int)lane < rem) tq = sp[32 * full_runs + lane];
+                                __syncwarp();
+                                if ((int)lane < rem) sp[lane] = tq;
+                            } else {
+                                T tv{};
+                                int32_t ti = 0;
+                                if ((int)lane < rem) {
+                                    if (VALS) tv = sv[32 * full_runs + lane];
+                                    if (IDX) ti = si[32 * full_runs + lane];
+                                }
+                                __syncwarp();
+                                if ((int)lane < rem) {
+                                    if (VALS) sv[lane] = tv;
+                                    if (IDX) si[lane] = ti;
+                                }
                             }
                             if (VALS) vbase += 32 * full_runs;
                             if (IDX) ibase += 32 * full_runs;
@@ -352,8 +385,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) compact_kernel(CompactAr
             if (full) rows_pass(std::true_type{});
             else rows_pass(std::false_type{});
             if ((int)lane >= lo && (int)lane < L) {  // the last, partial run
-                if (VALS) __stcs(vbase + lane, sv[lane]);
-                if (IDX) __stcs(ibase + lane, si[lane]);
+                if constexpr (kPack) {
+                    const uint2 q = sp[lane];
+                    __stcs(vbase + lane, ki::from_bits<T>(q.x));
+                    __stcs(ibase + lane, (int32_t)q.y);
+                } else {
+                    if (VALS) __stcs(vbase + lane, sv[lane]);
+                    if (IDX) __stcs(ibase + lane, si[lane]);
+                }
             }
             if (o.t == ntiles - 1 && w == 0 && lane == 0 && a.d_count) *a.d_count = (uint64_t)(o.tile_excl + o.agg);
         }

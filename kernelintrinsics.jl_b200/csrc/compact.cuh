@@ -36,6 +36,9 @@
 // written by bulk copies from the stage (each row then waits for its copy to read the stage) 0.70.
 // Without the barrier at the end of each iteration (the next ticket delivered through the tile
 // mbarrier, three pending-tile slots) 0.518 ms, and 0.438 with two CTAs of 16 warps.
+// Taking each ticket one fetch early and bulk-prefetching its tile into L2 (so that the tile's
+// load later hits L2): 0.549 ms; a tile then waits longer for its count, and so do the lookbacks
+// of the tiles after it.
 // Second-pass reads hit L2 only while at most about 96 KiB of tiles per SM are in flight (48 KiB
 // tiles x 2 CTAs of 16 warps, 32 KiB x 3 CTAs, 36 KiB x 3 CTAs of 12 warps), and each of those
 // shapes is slower (0.47-0.51 ms): fewer bytes or warps in flight cost more than the re-reads.

@@ -30,8 +30,8 @@
 // four popc and batches of 8; packed slots with batches of 8 spill: 0.443).  Writing each row's run
 // out on its own (unaligned 4-byte stores, most lines written in two parts by two store
 // instructions) took 0.471 ms; with whole aligned lines (and the two stage arrays), plain stores in
-// place of evict-first ones 0.443, an evict-last tile
-// load with evict-first second reads 0.474, no L2 prefetch 0.510, two CTAs of 16 warps over 8-row
+// place of evict-first ones 0.443, an evict-last tile load with evict-first second reads 0.474, no
+// L2 prefetch 0.510, two CTAs of 16 warps over 8-row
 // spans 0.437, batches of 4 rows 0.437, lookback windows of 64 / 128 tiles 0.439 / 0.454, runs
 // written by bulk copies from the stage (each row then waits for its copy to read the stage) 0.70.
 // Without the barrier at the end of each iteration (the next ticket delivered through the tile
@@ -47,8 +47,8 @@
 // without the stores the kernel takes 0.235 ms.  Writing the output streams evicts tiles that wait
 // for their prefix, so most second-pass reads come back from DRAM; the prefetch turns them into one
 // asynchronous bulk read per tile (0.51 -> 0.47 ms).  Slower alternatives: an evict-last or
-// evict-first hint on the first read (also
-// with the lines demoted to normal priority after the second read: 0.48 ms), evict-first second
+// evict-first hint on the first read (also with the lines demoted to normal priority after the
+// second read: 0.48 ms), evict-first second
 // reads (0.50), tiles kept in shared memory (two or three buffers, fewer CTAs per SM), 4096/8192-
 // element tiles, one CTA per SM of 16 or 24 work warps over 128/192 KiB tiles (0.52-0.54), two CTAs
 // per SM of 16 warps over 64 KiB tiles (0.47-0.48), 16 rows in flight per warp in the second pass
@@ -69,7 +69,8 @@
 // the DRAM bytes are the algorithmic ones, but each CTA then waits for its tile's prefix, and the
 // lookback chain over the ~150 tiles in flight sets the pace.  Every variant was checked against
 // this kernel's output (small, partial, misaligned and 2^28 inputs) before timing.  The kernel is
-// latency-bound (ncu at 2^26: DRAM 59 %, issue 52 %, warps 41 % active, stalls mostly at barriers).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
+// latency-bound (ncu at 2^26: DRAM 65 %, issue 50 %, warps 41 % active, stalls mostly at
+// barriers).  KI_COMPACT_WORK_WARPS, KI_COMPACT_ROWS and KI_COMPACT_CTAS_PER_SM set the shape.
 #pragma once
 
 #include "ki/common.cuh"

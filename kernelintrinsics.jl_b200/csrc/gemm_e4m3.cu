@@ -180,6 +180,7 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity, uint32
 // / 20 / 24 m blocks 2550 / 2633 / 2756 / 2708 / 2666, groups of 8 / 16 n blocks 2718 / 2724.
 // With evict-first C stores (the A and B panels keep more of L2): groups of 16 / 24 / 32 m blocks
 // 2847 / 2778 / 2654 on one box, and 2765 -> 2780-2794 against plain C stores on another.
+// Evict-last hints on the A or the B tile loads as well: 2702 / 2682 against 2708-2750 without.
 #ifndef KI_GEMM_GROUP_M
 #define KI_GEMM_GROUP_M 16  // 0: one group of all m blocks; negative: groups of n blocks
 #endif

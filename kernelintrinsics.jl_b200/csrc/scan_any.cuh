@@ -46,6 +46,9 @@ constexpr int kThreads = kWorkThreads + 32;
 // the copy peak, UInt8 cumsum / Int8 accumulate(max) / UInt8 accumulate(|)): 2 rows 0.41 / 0.25 /
 // 0.35, 4 rows 0.42 / 0.31 / 0.46, 8 rows 0.41 / 0.34 / 0.52, 12 rows 0.39 / 0.33 / 0.48, 14 rows
 // 0.38 / 0.34 / 0.50: the tile size is not what holds these back.
+// Two 16-byte vectors per lane and step for 4- and 8-byte elements (one warp scan per 2*kE
+// elements a lane, lanes 32 bytes apart) was slower everywhere at 2^28: Float32 cumsum 0.76 -> 0.66,
+// Int32 -> Int64 cumsum 0.84 -> 0.68, Float64 cumsum 0.72 -> 0.69, Int32 xor 0.89 -> 0.81.
 #ifndef KI_SCAN_ANY_PACK_F32
 #define KI_SCAN_ANY_PACK_F32 1
 #endif

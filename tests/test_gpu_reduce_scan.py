@@ -45,6 +45,44 @@ def test_reduce_config_size_pinned_to_host_generator(KI, oracle, dev):
     assert abs(got - ref) <= 1e-9 * ref  # in practice Float64-accurate
 
 
+def test_reduce_back_to_back_overlapped_launches(KI, oracle, dev):
+    """Reduces launched back to back (in a CUDA graph, where each launch's dispatch and L2
+    prefetches overlap the previous launch) give the bits of one reduce at a time, also when the
+    kernel before a reduce rewrites that reduce's input (the reduce must wait for it)."""
+    import torch
+
+    n = (1 << 22) + 3
+    xs = [torch.empty(n, dtype=torch.float32, device=dev) for _ in range(4)]
+    for k, x in enumerate(xs):
+        KI.fill_uniform(x, seed=40 + k)
+    want = [KI.warpfold_reduce(x).item() for x in xs]
+    outs = [torch.empty((), dtype=torch.float64, device=dev) for _ in range(12)]
+    refill = [torch.empty((), dtype=torch.float64, device=dev) for _ in range(4)]
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cs):
+        KI.warpfold_reduce(xs[0], out_f64=outs[0])  # warm-up on the capture stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=cs):
+            for j in range(12):  # reduce after reduce
+                KI.warpfold_reduce(xs[j % 4], out_f64=outs[j])
+            for k in range(4):  # a fill of the very input the next reduce reads
+                KI.fill_uniform(xs[k], seed=60 + k)
+                KI.warpfold_reduce(xs[k], out_f64=refill[k])
+    for _ in range(3):
+        for k, x in enumerate(xs):  # restore the first inputs before each replay
+            KI.fill_uniform(x, seed=40 + k)
+        g.replay()
+        torch.cuda.synchronize()
+        assert [o.item() for o in outs] == [want[j % 4] for j in range(12)]
+        for k in range(4):
+            ref = oracle.sum_f32(oracle.gen_uniform_f32(60 + k, n))
+            assert abs(refill[k].item() - ref) <= _tol(n) * ref
+            assert refill[k].item() == KI.warpfold_reduce(xs[k]).item()
+    del g
+
+
 def test_reduce_empty_and_special(KI, dev):
     import torch
 

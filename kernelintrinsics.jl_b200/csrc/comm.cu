@@ -90,6 +90,9 @@ struct XArgs {
 
 __global__ void __launch_bounds__(32) exchange_kernel(XArgs a) {
     __shared__ uint64_t vals[kMaxRanks];
+    // a kernel launched after this one with programmatic stream serialization (the next step's
+    // reduce) may be dispatched now; it waits for this kernel to complete before touching memory
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = (int)threadIdx.x;
     const uint64_t v = *a.local;
     uint64_t e = 0;

@@ -89,6 +89,10 @@ struct Pending {
 __device__ __forceinline__ void work_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkThreads) : "memory"); }
 
 __global__ void __launch_bounds__(kThreads) scan_i64_kernel(ScanArgs a) {
+    // every CTA of this persistent grid is resident from the start, so a dependent kernel launched
+    // with programmatic stream serialization (a sharded scan's next phase-1 reduce) may be
+    // dispatched as CTAs retire; it waits for this kernel to complete before touching memory
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(128) unsigned char smem_raw[];
     int64_t* sb = reinterpret_cast<int64_t*>(smem_raw);
     __shared__ __align__(8) uint64_t bar;

@@ -49,6 +49,12 @@ constexpr int kThreads = kWorkThreads + 32;
 // Two 16-byte vectors per lane and step for 4- and 8-byte elements (one warp scan per 2*kE
 // elements a lane, lanes 32 bytes apart) was slower everywhere at 2^28: Float32 cumsum 0.76 -> 0.66,
 // Int32 -> Int64 cumsum 0.84 -> 0.68, Float64 cumsum 0.72 -> 0.69, Int32 xor 0.89 -> 0.81.
+#ifndef KI_SCAN_ANY_SWAR_ALLROWS
+#define KI_SCAN_ANY_SWAR_ALLROWS 1
+#endif
+#ifndef KI_SCAN_ANY_SWAR
+#define KI_SCAN_ANY_SWAR 1
+#endif
 #ifndef KI_SCAN_ANY_PACK_F32
 #define KI_SCAN_ANY_PACK_F32 1
 #endif
@@ -93,6 +99,57 @@ struct Stage {
         return kChunks == 8 ? (q ^ (l & 7)) : ((q + (l >> 1)) & 3);
     }
 };
+
+// 1-byte elements whose scan keeps the element type (|, & and xor over Int8 / UInt8, max and min
+// over Int8): four elements per 32-bit word at once (SWAR).  comb combines the four byte lanes of
+// two words; kId is the operator's identity in every byte.  A word's inclusive prefix takes two
+// shifted combines; a lane's four words are chained by broadcasting each word's last byte.  With all
+// 8 rows of a warp's span in flight (the generic path takes 2 at a time) this took UInt8
+// accumulate(|), (&), (xor) from 0.44-0.46 to 0.61 of the copy peak at 2^28 and Int8 max / min from
+// 0.29 to 0.34-0.35; the same for UInt8 max / min (__vmaxu4 / __vminu4) was slower (0.38 -> 0.35),
+// so those keep the element-by-element path.
+template <class T, class Op>
+struct Swar {
+    static constexpr bool kOn = false;
+};
+template <class T, class Op, uint32_t ID>
+struct SwarBase {
+    static constexpr bool kOn = KI_SCAN_ANY_SWAR != 0;
+    static constexpr uint32_t kId = ID * 0x01010101u;
+    __device__ static __forceinline__ uint32_t bcast(uint32_t b) { return (b & 0xFFu) * 0x01010101u; }
+};
+template <class T>
+struct Swar<T, ki::JOr> : SwarBase<T, ki::JOr, 0x00u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a | b; }
+};
+template <class T>
+struct Swar<T, ki::JAnd> : SwarBase<T, ki::JAnd, 0xFFu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a & b; }
+};
+template <class T>
+struct Swar<T, ki::JXor> : SwarBase<T, ki::JXor, 0x00u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a ^ b; }
+};
+template <>
+struct Swar<int8_t, ki::JMax> : SwarBase<int8_t, ki::JMax, 0x80u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
+};
+template <>
+struct Swar<int8_t, ki::JMin> : SwarBase<int8_t, ki::JMin, 0x7Fu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins4(a, b); }
+};
+// only for 1-byte elements whose result keeps the type
+template <class T, class Op>
+constexpr bool swar_on() {
+    if constexpr (sizeof(T) == 1 && std::is_same<typename ki::Traits<T, Op>::R, T>::value) return Swar<T, Op>::kOn;
+    else return false;
+}
+// inclusive prefix of the four byte lanes of w (byte 0 first)
+template <class SW>
+__device__ __forceinline__ uint32_t swar_prefix(uint32_t w) {
+    w = SW::comb(w, (w << 8) | (SW::kId & 0x000000FFu));
+    return SW::comb(w, (w << 16) | (SW::kId & 0x0000FFFFu));
+}
 
 // The input is rows x cols (rows = 1 for a plain scan): row r starts ld_in elements after row r-1
 // in the input and ld_out after it in the output, and every row is a segment of its own, cut into
@@ -212,12 +269,25 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 work_sync();
             }
             A s = id;
+            if constexpr (swar_on<T, Op>()) {
+                using SW = Swar<T, Op>;
+                uint32_t acc = SW::kId;
 #pragma unroll
-            for (int j = 0; j < S::kRows; ++j) {
-                ki::Packed16<T> v;
-                v.raw = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
+                for (int j = 0; j < S::kRows; ++j) {
+                    const uint4 r = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
+                    acc = SW::comb(acc, SW::comb(SW::comb(r.x, r.y), SW::comb(r.z, r.w)));
+                }
+                acc = SW::comb(acc, (acc >> 16) | (SW::kId & 0xFFFF0000u));
+                acc = SW::comb(acc, (acc >> 8) | (SW::kId & 0xFF000000u));
+                s = (A)(T)(acc & 0xFFu);
+            } else {
 #pragma unroll
-                for (int e = 0; e < kE; ++e) s = op(s, Tr::lift(v.get(e)));
+                for (int j = 0; j < S::kRows; ++j) {
+                    ki::Packed16<T> v;
+                    v.raw = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
+#pragma unroll
+                    for (int e = 0; e < kE; ++e) s = op(s, Tr::lift(v.get(e)));
+                }
             }
             s = ki::warpfold(s, op);
             if (lane == 0) warp_tot[w] = s;
@@ -251,7 +321,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             const T pad = ki::pad_value<T, Op>();
             // rows in flight: all 8 for 4- and 8-byte elements; 1- and 2-byte elements take more
             // registers per row on the way out, so they go KI_SCAN_ANY_SMALL_BATCH rows at a time
-            constexpr int kB = sizeof(T) >= 4 ? S::kRows : (KI_SCAN_ANY_SMALL_BATCH < S::kRows ? KI_SCAN_ANY_SMALL_BATCH : S::kRows);
+            constexpr int kB = (sizeof(T) >= 4 || (swar_on<T, Op>() && KI_SCAN_ANY_SWAR_ALLROWS)) ? S::kRows
+                               : (KI_SCAN_ANY_SMALL_BATCH < S::kRows ? KI_SCAN_ANY_SMALL_BATCH : S::kRows);
             static_assert(S::kRows % kB == 0, "row batches");
 #pragma unroll 1
             for (int j0 = 0; j0 < S::kRows; j0 += kB) {
@@ -272,6 +343,38 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 const int j = j0 + jj;
                 // the lane's total, the warp's scan of the totals, then the lane's prefixes again on
                 // the way out (no per-element arrays: 16-byte lanes of 1-byte elements stay in registers)
+                if constexpr (swar_on<T, Op>()) {
+                    using SW = Swar<T, Op>;
+                    uint32_t y0 = swar_prefix<SW>(v[jj].raw.x), y1 = swar_prefix<SW>(v[jj].raw.y);
+                    uint32_t y2 = swar_prefix<SW>(v[jj].raw.z), y3 = swar_prefix<SW>(v[jj].raw.w);
+                    y1 = SW::comb(y1, SW::bcast(y0 >> 24));
+                    y2 = SW::comb(y2, SW::bcast(y1 >> 24));
+                    y3 = SW::comb(y3, SW::bcast(y2 >> 24));
+                    const A tot = (A)(T)(y3 >> 24);
+                    const A inc = ki::warpreduce(tot, op);
+                    A before = __shfl_up_sync(0xffffffffu, inc, 1);
+                    if (lane == 0) before = id;
+                    const A run = op(carry, before);
+                    const uint32_t rb = SW::bcast((uint32_t)(uint8_t)run);
+                    uint32_t o0 = SW::comb(y0, rb), o1 = SW::comb(y1, rb), o2 = SW::comb(y2, rb), o3 = SW::comb(y3, rb);
+                    if (EXCL) {  // shift by one element: the first is the running prefix
+                        o3 = (o3 << 8) | (o2 >> 24);
+                        o2 = (o2 << 8) | (o1 >> 24);
+                        o1 = (o1 << 8) | (o0 >> 24);
+                        o0 = (o0 << 8) | (rb & 0xFFu);
+                    }
+                    const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
+                    if (full && a.vec_out) {
+                        __stcs(reinterpret_cast<uint4*>(out + out_first + i), make_uint4(o0, o1, o2, o3));
+                    } else {
+                        const uint32_t o[4] = {o0, o1, o2, o3};
+#pragma unroll
+                        for (int e = 0; e < kE; ++e)
+                            if (i + e < count) out[out_first + i + e] = (R)(T)((o[e >> 2] >> (8 * (e & 3))) & 0xFFu);
+                    }
+                    carry = op(carry, __shfl_sync(0xffffffffu, inc, 31));
+                    continue;
+                }
                 A tot = Tr::lift(v[jj].get(0));
 #pragma unroll
                 for (int e = 1; e < kE; ++e) tot = op(tot, Tr::lift(v[jj].get(e)));

@@ -155,6 +155,9 @@ __device__ __forceinline__ T highest_of() {
 // the key that wins (all ones for max, zero for min), so max/min of floats run as integer
 // max/min: one instruction per step instead of Base.max's select chain.  Keys are converted back
 // once, at the output (a NaN result comes back as the canonical quiet NaN).
+// Compares and selects on the values themselves (NaN checks, then the signed-zero tie) were
+// slower: Float32 accumulate(max) 0.62 -> 0.36 of the copy peak, Float64 0.52 -> 0.37, the
+// Float32 / Float64 maximum reduce 1.01 -> 0.97.
 template <class F>
 struct FloatKey {
     using K = typename std::conditional<sizeof(F) == 4, uint32_t, uint64_t>::type;

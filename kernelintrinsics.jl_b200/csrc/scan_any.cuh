@@ -52,6 +52,9 @@ constexpr int kThreads = kWorkThreads + 32;
 #ifndef KI_SCAN_ANY_SWAR_ALLROWS
 #define KI_SCAN_ANY_SWAR_ALLROWS 1
 #endif
+#ifndef KI_SCAN_ANY_SWAR16_MAXMIN
+#define KI_SCAN_ANY_SWAR16_MAXMIN 1
+#endif
 #ifndef KI_SCAN_ANY_SWAR
 #define KI_SCAN_ANY_SWAR 1
 #endif
@@ -100,30 +103,36 @@ struct Stage {
     }
 };
 
-// 1-byte elements whose scan keeps the element type (|, & and xor over Int8 / UInt8, max and min
-// over Int8): four elements per 32-bit word at once (SWAR).  comb combines the four byte lanes of
-// two words; kId is the operator's identity in every byte.  A word's inclusive prefix takes two
-// shifted combines; a lane's four words are chained by broadcasting each word's last byte.  With all
-// 8 rows of a warp's span in flight (the generic path takes 2 at a time) this took UInt8
-// accumulate(|), (&), (xor) from 0.44-0.46 to 0.61 of the copy peak at 2^28 and Int8 max / min from
-// 0.29 to 0.34-0.35; the same for UInt8 max / min (__vmaxu4 / __vminu4) was slower (0.38 -> 0.35),
-// so those keep the element-by-element path.
+// 1- and 2-byte elements whose scan keeps the element type (|, & and xor; max and min where the
+// byte or halfword SIMD form pays): four or two elements per 32-bit word at once (SWAR).  comb
+// combines the element lanes of two words; kId is the operator's identity in every lane.  A word's
+// inclusive prefix takes one shifted combine per doubling; a lane's four words are chained by
+// broadcasting each word's last element.  With all 8 rows of a warp's span in flight (the generic
+// path takes 2 at a time) this took UInt8 accumulate(|), (&), (xor) from 0.44-0.46 to 0.61 of the
+// copy peak at 2^28 and Int8 max / min from 0.29 to 0.34-0.35; the same for UInt8 max / min
+// (__vmaxu4 / __vminu4) was slower (0.38 -> 0.35), so those keep the element-by-element path.
+// Halfwords (Int16 / UInt16, __vmaxs2 / __vmaxu2 / __vmins2 / __vminu2 for max / min): |, &, xor
+// 0.66 -> 0.77-0.79, max / min 0.61-0.62 -> 0.75-0.77.
 template <class T, class Op>
 struct Swar {
     static constexpr bool kOn = false;
 };
 template <class T, class Op, uint32_t ID>
 struct SwarBase {
+    static_assert(sizeof(T) == 1 || sizeof(T) == 2, "byte or halfword lanes");
     static constexpr bool kOn = KI_SCAN_ANY_SWAR != 0;
-    static constexpr uint32_t kId = ID * 0x01010101u;
-    __device__ static __forceinline__ uint32_t bcast(uint32_t b) { return (b & 0xFFu) * 0x01010101u; }
+    static constexpr int kBits = 8 * (int)sizeof(T);                      // bits per element
+    static constexpr uint32_t kRep = sizeof(T) == 1 ? 0x01010101u : 0x00010001u;
+    static constexpr uint32_t kMask = sizeof(T) == 1 ? 0xFFu : 0xFFFFu;
+    static constexpr uint32_t kId = ID * kRep;
+    __device__ static __forceinline__ uint32_t bcast(uint32_t e) { return (e & kMask) * kRep; }
 };
 template <class T>
 struct Swar<T, ki::JOr> : SwarBase<T, ki::JOr, 0x00u> {
     __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a | b; }
 };
 template <class T>
-struct Swar<T, ki::JAnd> : SwarBase<T, ki::JAnd, 0xFFu> {
+struct Swar<T, ki::JAnd> : SwarBase<T, ki::JAnd, (sizeof(T) == 1 ? 0xFFu : 0xFFFFu)> {
     __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a & b; }
 };
 template <class T>
@@ -138,17 +147,36 @@ template <>
 struct Swar<int8_t, ki::JMin> : SwarBase<int8_t, ki::JMin, 0x7Fu> {
     __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins4(a, b); }
 };
-// only for 1-byte elements whose result keeps the type
+#if KI_SCAN_ANY_SWAR16_MAXMIN
+template <>
+struct Swar<int16_t, ki::JMax> : SwarBase<int16_t, ki::JMax, 0x8000u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs2(a, b); }
+};
+template <>
+struct Swar<int16_t, ki::JMin> : SwarBase<int16_t, ki::JMin, 0x7FFFu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins2(a, b); }
+};
+template <>
+struct Swar<uint16_t, ki::JMax> : SwarBase<uint16_t, ki::JMax, 0x0000u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
+};
+template <>
+struct Swar<uint16_t, ki::JMin> : SwarBase<uint16_t, ki::JMin, 0xFFFFu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vminu2(a, b); }
+};
+#endif
+// only for 1- and 2-byte elements whose result keeps the type
 template <class T, class Op>
 constexpr bool swar_on() {
-    if constexpr (sizeof(T) == 1 && std::is_same<typename ki::Traits<T, Op>::R, T>::value) return Swar<T, Op>::kOn;
+    if constexpr (sizeof(T) <= 2 && std::is_same<typename ki::Traits<T, Op>::R, T>::value) return Swar<T, Op>::kOn;
     else return false;
 }
-// inclusive prefix of the four byte lanes of w (byte 0 first)
+// inclusive prefix of the element lanes of w (lowest lane first)
 template <class SW>
 __device__ __forceinline__ uint32_t swar_prefix(uint32_t w) {
-    w = SW::comb(w, (w << 8) | (SW::kId & 0x000000FFu));
-    return SW::comb(w, (w << 16) | (SW::kId & 0x0000FFFFu));
+#pragma unroll
+    for (int s = SW::kBits; s < 32; s <<= 1) w = SW::comb(w, (w << s) | (SW::kId & ((1u << s) - 1u)));
+    return w;
 }
 
 // The input is rows x cols (rows = 1 for a plain scan): row r starts ld_in elements after row r-1
@@ -277,9 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                     const uint4 r = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
                     acc = SW::comb(acc, SW::comb(SW::comb(r.x, r.y), SW::comb(r.z, r.w)));
                 }
-                acc = SW::comb(acc, (acc >> 16) | (SW::kId & 0xFFFF0000u));
-                acc = SW::comb(acc, (acc >> 8) | (SW::kId & 0xFF000000u));
-                s = (A)(T)(acc & 0xFFu);
+#pragma unroll
+                for (int sh = 16; sh >= SW::kBits; sh >>= 1) acc = SW::comb(acc, (acc >> sh) | (SW::kId & ~(0xFFFFFFFFu >> sh)));
+                s = (A)(T)(acc & SW::kMask);
             } else {
 #pragma unroll
                 for (int j = 0; j < S::kRows; ++j) {
@@ -347,21 +375,22 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                     using SW = Swar<T, Op>;
                     uint32_t y0 = swar_prefix<SW>(v[jj].raw.x), y1 = swar_prefix<SW>(v[jj].raw.y);
                     uint32_t y2 = swar_prefix<SW>(v[jj].raw.z), y3 = swar_prefix<SW>(v[jj].raw.w);
-                    y1 = SW::comb(y1, SW::bcast(y0 >> 24));
-                    y2 = SW::comb(y2, SW::bcast(y1 >> 24));
-                    y3 = SW::comb(y3, SW::bcast(y2 >> 24));
-                    const A tot = (A)(T)(y3 >> 24);
+                    constexpr int kTop = 32 - SW::kBits;  // shift of a word's last element
+                    y1 = SW::comb(y1, SW::bcast(y0 >> kTop));
+                    y2 = SW::comb(y2, SW::bcast(y1 >> kTop));
+                    y3 = SW::comb(y3, SW::bcast(y2 >> kTop));
+                    const A tot = (A)(T)(y3 >> kTop);
                     const A inc = ki::warpreduce(tot, op);
                     A before = __shfl_up_sync(0xffffffffu, inc, 1);
                     if (lane == 0) before = id;
                     const A run = op(carry, before);
-                    const uint32_t rb = SW::bcast((uint32_t)(uint8_t)run);
+                    const uint32_t rb = SW::bcast((uint32_t)(typename std::make_unsigned<T>::type)run);
                     uint32_t o0 = SW::comb(y0, rb), o1 = SW::comb(y1, rb), o2 = SW::comb(y2, rb), o3 = SW::comb(y3, rb);
                     if (EXCL) {  // shift by one element: the first is the running prefix
-                        o3 = (o3 << 8) | (o2 >> 24);
-                        o2 = (o2 << 8) | (o1 >> 24);
-                        o1 = (o1 << 8) | (o0 >> 24);
-                        o0 = (o0 << 8) | (rb & 0xFFu);
+                        o3 = (o3 << SW::kBits) | (o2 >> kTop);
+                        o2 = (o2 << SW::kBits) | (o1 >> kTop);
+                        o1 = (o1 << SW::kBits) | (o0 >> kTop);
+                        o0 = (o0 << SW::kBits) | (rb & SW::kMask);
                     }
                     const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
                     if (full && a.vec_out) {
@@ -370,7 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                         const uint32_t o[4] = {o0, o1, o2, o3};
 #pragma unroll
                         for (int e = 0; e < kE; ++e)
-                            if (i + e < count) out[out_first + i + e] = (R)(T)((o[e >> 2] >> (8 * (e & 3))) & 0xFFu);
+                            if (i + e < count) {
+                                constexpr int kPer = 32 / SW::kBits;  // elements per word
+                                out[out_first + i + e] = (R)(T)((o[e / kPer] >> (SW::kBits * (e % kPer))) & SW::kMask);
+                            }
                     }
                     carry = op(carry, __shfl_sync(0xffffffffu, inc, 31));
                     continue;

@@ -332,4 +332,86 @@ struct Packed16 {
     }
 };
 
+#ifndef KI_SWAR
+#define KI_SWAR 1
+#endif
+#ifndef KI_SWAR16_MAXMIN
+#define KI_SWAR16_MAXMIN 1
+#endif
+// 1- and 2-byte elements whose scan or reduce keeps the element type (|, & and xor; max and min where the
+// byte or halfword SIMD form pays): four or two elements per 32-bit word at once (SWAR).  comb
+// combines the element lanes of two words; kId is the operator's identity in every lane.  A word's
+// inclusive prefix takes one shifted combine per doubling; a lane's four words are chained by
+// broadcasting each word's last element.  With all 8 rows of a warp's span in flight (the generic
+// path takes 2 at a time) this took UInt8 accumulate(|), (&), (xor) from 0.44-0.46 to 0.61 of the
+// copy peak at 2^28 and Int8 max / min from 0.29 to 0.34-0.35; the same for UInt8 max / min
+// (__vmaxu4 / __vminu4) was slower (0.38 -> 0.35), so those keep the element-by-element path.
+// Halfwords (Int16 / UInt16, __vmaxs2 / __vmaxu2 / __vmins2 / __vminu2 for max / min): |, &, xor
+// 0.66 -> 0.77-0.79, max / min 0.61-0.62 -> 0.75-0.77.
+template <class T, class Op>
+struct Swar {
+    static constexpr bool kOn = false;
+};
+template <class T, class Op, uint32_t ID>
+struct SwarBase {
+    static_assert(sizeof(T) == 1 || sizeof(T) == 2, "byte or halfword lanes");
+    static constexpr bool kOn = KI_SWAR != 0;
+    static constexpr int kBits = 8 * (int)sizeof(T);                      // bits per element
+    static constexpr uint32_t kRep = sizeof(T) == 1 ? 0x01010101u : 0x00010001u;
+    static constexpr uint32_t kMask = sizeof(T) == 1 ? 0xFFu : 0xFFFFu;
+    static constexpr uint32_t kId = ID * kRep;
+    __device__ static __forceinline__ uint32_t bcast(uint32_t e) { return (e & kMask) * kRep; }
+};
+template <class T>
+struct Swar<T, JOr> : SwarBase<T, JOr, 0x00u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a | b; }
+};
+template <class T>
+struct Swar<T, JAnd> : SwarBase<T, JAnd, (sizeof(T) == 1 ? 0xFFu : 0xFFFFu)> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a & b; }
+};
+template <class T>
+struct Swar<T, JXor> : SwarBase<T, JXor, 0x00u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a ^ b; }
+};
+template <>
+struct Swar<int8_t, JMax> : SwarBase<int8_t, JMax, 0x80u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
+};
+template <>
+struct Swar<int8_t, JMin> : SwarBase<int8_t, JMin, 0x7Fu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins4(a, b); }
+};
+#if KI_SWAR16_MAXMIN
+template <>
+struct Swar<int16_t, JMax> : SwarBase<int16_t, JMax, 0x8000u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs2(a, b); }
+};
+template <>
+struct Swar<int16_t, JMin> : SwarBase<int16_t, JMin, 0x7FFFu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins2(a, b); }
+};
+template <>
+struct Swar<uint16_t, JMax> : SwarBase<uint16_t, JMax, 0x0000u> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
+};
+template <>
+struct Swar<uint16_t, JMin> : SwarBase<uint16_t, JMin, 0xFFFFu> {
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vminu2(a, b); }
+};
+#endif
+// only for 1- and 2-byte elements whose result keeps the type
+template <class T, class Op>
+constexpr bool swar_on() {
+    if constexpr (sizeof(T) <= 2 && std::is_same<typename Traits<T, Op>::R, T>::value) return Swar<T, Op>::kOn;
+    else return false;
+}
+// inclusive prefix of the element lanes of w (lowest lane first)
+template <class SW>
+__device__ __forceinline__ uint32_t swar_prefix(uint32_t w) {
+#pragma unroll
+    for (int s = SW::kBits; s < 32; s <<= 1) w = SW::comb(w, (w << s) | (SW::kId & ((1u << s) - 1u)));
+    return w;
+}
+
 }  // namespace ki

@@ -64,6 +64,14 @@ __device__ __forceinline__ typename ki::Traits<T, Op>::A fold_vec(const ki::Pack
     constexpr int kV = (int)(16 / sizeof(T));
     if constexpr (std::is_same<T, float>::value && std::is_same<Op, ki::JAdd>::value) {
         return (double)((M::apply(v.get(0)) + M::apply(v.get(1))) + (M::apply(v.get(2)) + M::apply(v.get(3))));
+    } else if constexpr (std::is_same<M, ki::MapId>::value && ki::swar_on<T, Op>()) {
+        // 1- and 2-byte elements that keep their type: the four words are combined lane-wise
+        // (SWAR), then the lanes of the one word left
+        using SW = ki::Swar<T, Op>;
+        uint32_t w = SW::comb(SW::comb(v.raw.x, v.raw.y), SW::comb(v.raw.z, v.raw.w));
+#pragma unroll
+        for (int sh = 16; sh >= SW::kBits; sh >>= 1) w = SW::comb(w, (w >> sh) | (SW::kId & ~(0xFFFFFFFFu >> sh)));
+        return (A)(T)(w & SW::kMask);
     } else {
         A r = Tr::lift(M::apply(v.get(0)));
 #pragma unroll

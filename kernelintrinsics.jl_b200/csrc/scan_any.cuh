@@ -52,12 +52,6 @@ constexpr int kThreads = kWorkThreads + 32;
 #ifndef KI_SCAN_ANY_SWAR_ALLROWS
 #define KI_SCAN_ANY_SWAR_ALLROWS 1
 #endif
-#ifndef KI_SCAN_ANY_SWAR16_MAXMIN
-#define KI_SCAN_ANY_SWAR16_MAXMIN 1
-#endif
-#ifndef KI_SCAN_ANY_SWAR
-#define KI_SCAN_ANY_SWAR 1
-#endif
 #ifndef KI_SCAN_ANY_PACK_F32
 #define KI_SCAN_ANY_PACK_F32 1
 #endif
@@ -102,82 +96,6 @@ struct Stage {
         return kChunks == 8 ? (q ^ (l & 7)) : ((q + (l >> 1)) & 3);
     }
 };
-
-// 1- and 2-byte elements whose scan keeps the element type (|, & and xor; max and min where the
-// byte or halfword SIMD form pays): four or two elements per 32-bit word at once (SWAR).  comb
-// combines the element lanes of two words; kId is the operator's identity in every lane.  A word's
-// inclusive prefix takes one shifted combine per doubling; a lane's four words are chained by
-// broadcasting each word's last element.  With all 8 rows of a warp's span in flight (the generic
-// path takes 2 at a time) this took UInt8 accumulate(|), (&), (xor) from 0.44-0.46 to 0.61 of the
-// copy peak at 2^28 and Int8 max / min from 0.29 to 0.34-0.35; the same for UInt8 max / min
-// (__vmaxu4 / __vminu4) was slower (0.38 -> 0.35), so those keep the element-by-element path.
-// Halfwords (Int16 / UInt16, __vmaxs2 / __vmaxu2 / __vmins2 / __vminu2 for max / min): |, &, xor
-// 0.66 -> 0.77-0.79, max / min 0.61-0.62 -> 0.75-0.77.
-template <class T, class Op>
-struct Swar {
-    static constexpr bool kOn = false;
-};
-template <class T, class Op, uint32_t ID>
-struct SwarBase {
-    static_assert(sizeof(T) == 1 || sizeof(T) == 2, "byte or halfword lanes");
-    static constexpr bool kOn = KI_SCAN_ANY_SWAR != 0;
-    static constexpr int kBits = 8 * (int)sizeof(T);                      // bits per element
-    static constexpr uint32_t kRep = sizeof(T) == 1 ? 0x01010101u : 0x00010001u;
-    static constexpr uint32_t kMask = sizeof(T) == 1 ? 0xFFu : 0xFFFFu;
-    static constexpr uint32_t kId = ID * kRep;
-    __device__ static __forceinline__ uint32_t bcast(uint32_t e) { return (e & kMask) * kRep; }
-};
-template <class T>
-struct Swar<T, ki::JOr> : SwarBase<T, ki::JOr, 0x00u> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a | b; }
-};
-template <class T>
-struct Swar<T, ki::JAnd> : SwarBase<T, ki::JAnd, (sizeof(T) == 1 ? 0xFFu : 0xFFFFu)> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a & b; }
-};
-template <class T>
-struct Swar<T, ki::JXor> : SwarBase<T, ki::JXor, 0x00u> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a ^ b; }
-};
-template <>
-struct Swar<int8_t, ki::JMax> : SwarBase<int8_t, ki::JMax, 0x80u> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
-};
-template <>
-struct Swar<int8_t, ki::JMin> : SwarBase<int8_t, ki::JMin, 0x7Fu> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins4(a, b); }
-};
-#if KI_SCAN_ANY_SWAR16_MAXMIN
-template <>
-struct Swar<int16_t, ki::JMax> : SwarBase<int16_t, ki::JMax, 0x8000u> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs2(a, b); }
-};
-template <>
-struct Swar<int16_t, ki::JMin> : SwarBase<int16_t, ki::JMin, 0x7FFFu> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins2(a, b); }
-};
-template <>
-struct Swar<uint16_t, ki::JMax> : SwarBase<uint16_t, ki::JMax, 0x0000u> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
-};
-template <>
-struct Swar<uint16_t, ki::JMin> : SwarBase<uint16_t, ki::JMin, 0xFFFFu> {
-    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vminu2(a, b); }
-};
-#endif
-// only for 1- and 2-byte elements whose result keeps the type
-template <class T, class Op>
-constexpr bool swar_on() {
-    if constexpr (sizeof(T) <= 2 && std::is_same<typename ki::Traits<T, Op>::R, T>::value) return Swar<T, Op>::kOn;
-    else return false;
-}
-// inclusive prefix of the element lanes of w (lowest lane first)
-template <class SW>
-__device__ __forceinline__ uint32_t swar_prefix(uint32_t w) {
-#pragma unroll
-    for (int s = SW::kBits; s < 32; s <<= 1) w = SW::comb(w, (w << s) | (SW::kId & ((1u << s) - 1u)));
-    return w;
-}
 
 // The input is rows x cols (rows = 1 for a plain scan): row r starts ld_in elements after row r-1
 // in the input and ld_out after it in the output, and every row is a segment of its own, cut into
@@ -297,8 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 work_sync();
             }
             A s = id;
-            if constexpr (swar_on<T, Op>()) {
-                using SW = Swar<T, Op>;
+            if constexpr (ki::swar_on<T, Op>()) {
+                using SW = ki::Swar<T, Op>;
                 uint32_t acc = SW::kId;
 #pragma unroll
                 for (int j = 0; j < S::kRows; ++j) {
@@ -349,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             const T pad = ki::pad_value<T, Op>();
             // rows in flight: all 8 for 4- and 8-byte elements; 1- and 2-byte elements take more
             // registers per row on the way out, so they go KI_SCAN_ANY_SMALL_BATCH rows at a time
-            constexpr int kB = (sizeof(T) >= 4 || (swar_on<T, Op>() && KI_SCAN_ANY_SWAR_ALLROWS)) ? S::kRows
+            constexpr int kB = (sizeof(T) >= 4 || (ki::swar_on<T, Op>() && KI_SCAN_ANY_SWAR_ALLROWS)) ? S::kRows
                                : (KI_SCAN_ANY_SMALL_BATCH < S::kRows ? KI_SCAN_ANY_SMALL_BATCH : S::kRows);
             static_assert(S::kRows % kB == 0, "row batches");
 #pragma unroll 1
@@ -371,10 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 const int j = j0 + jj;
                 // the lane's total, the warp's scan of the totals, then the lane's prefixes again on
                 // the way out (no per-element arrays: 16-byte lanes of 1-byte elements stay in registers)
-                if constexpr (swar_on<T, Op>()) {
-                    using SW = Swar<T, Op>;
-                    uint32_t y0 = swar_prefix<SW>(v[jj].raw.x), y1 = swar_prefix<SW>(v[jj].raw.y);
-                    uint32_t y2 = swar_prefix<SW>(v[jj].raw.z), y3 = swar_prefix<SW>(v[jj].raw.w);
+                if constexpr (ki::swar_on<T, Op>()) {
+                    using SW = ki::Swar<T, Op>;
+                    uint32_t y0 = ki::swar_prefix<SW>(v[jj].raw.x), y1 = ki::swar_prefix<SW>(v[jj].raw.y);
+                    uint32_t y2 = ki::swar_prefix<SW>(v[jj].raw.z), y3 = ki::swar_prefix<SW>(v[jj].raw.w);
                     constexpr int kTop = 32 - SW::kBits;  // shift of a word's last element
                     y1 = SW::comb(y1, SW::bcast(y0 >> kTop));
                     y2 = SW::comb(y2, SW::bcast(y1 >> kTop));

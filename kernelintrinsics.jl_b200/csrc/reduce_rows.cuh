@@ -13,6 +13,9 @@
 //     the row's partials in order.  Chunks per row are chosen so the grid fills the GPU even when
 //     there are few rows.
 // Both are deterministic for a given shape and device.
+// Folding 1-byte vectors lane-wise (SWAR, as the device-wide reduce does) gave mixed results here
+// (UInt8 | over 2^21 x 256: 0.40 -> 0.51 of the copy peak, Int8 maximum over 16384 x 65536: 0.81 ->
+// 0.78), so rows keep the element-by-element fold.
 #pragma once
 
 #include "ki/common.cuh"

@@ -109,6 +109,26 @@ def test_scan_init_misaligned_and_in_place(KI, oracle, dev, dt):
     KI.context(0).check()
 
 
+@pytest.mark.parametrize("dt", [np.int8, np.uint8, np.int16, np.uint16], ids=lambda d: np.dtype(d).name)
+def test_scan_narrow_same_type_misaligned(KI, oracle, dev, dt):
+    """1- and 2-byte scans that keep their type (lane-wise words inside the kernel) from inputs and
+    into outputs that are not 16-byte aligned, inclusive and exclusive, with and without init."""
+    import torch
+
+    n = 2 * 126976 + 37  # two full 1-byte tiles and a partial one
+    for off in (1, 3):
+        for op in ("|", "&", "xor", "max", "min"):
+            x = _data(dt, n + off, 11 + off, op)
+            xs = _to_dev(x, dev)[off:]
+            for excl in (False, True):
+                for init in (None, 3):
+                    out = torch.empty(n + off, dtype=xs.dtype, device=dev)[off:]
+                    got = KI.scan(xs, op, exclusive=excl, init=init, out=out).cpu().numpy()
+                    want = oracle.accumulate(op, x[off:], exclusive=excl, init=init)
+                    assert np.array_equal(got, want.astype(got.dtype)), (op, excl, init, off)
+    KI.context(0).check()
+
+
 def test_scan_nan_and_extremes(KI, oracle, dev):
     x = np.array([1.0, np.nan, -np.inf, 2.0, -0.0, 0.0] * 7000, dtype=np.float32)
     xd = _to_dev(x, dev)

@@ -338,14 +338,22 @@ struct Packed16 {
 #ifndef KI_SWAR16_MAXMIN
 #define KI_SWAR16_MAXMIN 1
 #endif
+#ifndef KI_SWAR8_MAXMIN
+#define KI_SWAR8_MAXMIN 1
+#endif
+#ifndef KI_SWAR8_SPLIT
+#define KI_SWAR8_SPLIT 1
+#endif
 // 1- and 2-byte elements whose scan or reduce keeps the element type (|, & and xor; max and min where the
 // byte or halfword SIMD form pays): four or two elements per 32-bit word at once (SWAR).  comb
 // combines the element lanes of two words; kId is the operator's identity in every lane.  A word's
 // inclusive prefix takes one shifted combine per doubling; a lane's four words are chained by
 // broadcasting each word's last element.  With all 8 rows of a warp's span in flight (the generic
 // path takes 2 at a time) this took UInt8 accumulate(|), (&), (xor) from 0.44-0.46 to 0.61 of the
-// copy peak at 2^28 and Int8 max / min from 0.29 to 0.34-0.35; the same for UInt8 max / min
-// (__vmaxu4 / __vminu4) was slower (0.38 -> 0.35), so those keep the element-by-element path.
+// copy peak at 2^28.  Byte max / min: with __vmaxs4 / __vmins4, Int8 0.29 -> 0.34-0.35 (__vmaxu4 for
+// UInt8 was slower than element by element, 0.38 -> 0.35); through the halfword instructions below
+// (SwarBytePair) Int8 0.42, UInt8 0.46-0.47, and with the scan keeping the words split until the
+// running prefix is in, Int8 0.465, UInt8 0.51-0.53, results identical.
 // Halfwords (Int16 / UInt16, __vmaxs2 / __vmaxu2 / __vmins2 / __vminu2 for max / min): |, &, xor
 // 0.66 -> 0.77-0.79, max / min 0.61-0.62 -> 0.75-0.77.
 template <class T, class Op>
@@ -360,7 +368,13 @@ struct SwarBase {
     static constexpr uint32_t kRep = sizeof(T) == 1 ? 0x01010101u : 0x00010001u;
     static constexpr uint32_t kMask = sizeof(T) == 1 ? 0xFFu : 0xFFFFu;
     static constexpr uint32_t kId = ID * kRep;
+    static constexpr bool kOwnPrefix = false;  // true where the operator has its own word prefix
+    static constexpr bool kSplit = false;      // true where scans keep the words split (byte max / min)
     __device__ static __forceinline__ uint32_t bcast(uint32_t e) { return (e & kMask) * kRep; }
+    // the word's last element in every lane (one byte permute)
+    __device__ static __forceinline__ uint32_t top(uint32_t w) {
+        return __byte_perm(w, 0u, sizeof(T) == 1 ? 0x3333u : 0x3232u);
+    }
 };
 template <class T>
 struct Swar<T, JOr> : SwarBase<T, JOr, 0x00u> {
@@ -374,6 +388,73 @@ template <class T>
 struct Swar<T, JXor> : SwarBase<T, JXor, 0x00u> {
     __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return a ^ b; }
 };
+#if KI_SWAR8_MAXMIN
+// Byte max / min through the halfword max / min instructions (max.s16x2 and the like, sm_90 and
+// later): for two halfwords whose high bytes are elements x and y, the larger (smaller) halfword has
+// the larger (smaller) of x and y as its high byte whatever the low bytes hold, since a low byte moves
+// a halfword by less than one step of its high byte.  So the odd bytes of a word take one halfword
+// instruction as they lie, the even bytes one after a shift by 8, and a byte permute puts the high
+// bytes back in place.  A word's inclusive prefix p0..p3 of bytes b0..b3 is four halfword
+// instructions: m = op(b0,b1) | op(b2,b3) (high bytes), s = m moved up a halfword over the identity,
+// op(m, s) = p1 | p3 and op(b0 | b2, s) = p0 | p2.
+template <class T, class Op, uint32_t ID>
+struct SwarBytePair : SwarBase<T, Op, ID> {
+    static constexpr bool kOwnPrefix = true;
+    static constexpr bool kSplit = KI_SWAR8_SPLIT != 0;
+    __device__ static __forceinline__ uint32_t h(uint32_t a, uint32_t b) {
+        uint32_t d;
+        if constexpr (std::is_same<Op, JMax>::value && std::is_signed<T>::value)
+            asm("max.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        else if constexpr (std::is_same<Op, JMax>::value)
+            asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        else if constexpr (std::is_signed<T>::value)
+            asm("min.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        else
+            asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+        return d;
+    }
+    __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) {
+        return __byte_perm(h(a << 8, b << 8), h(a, b), 0x7351u);
+    }
+    // the prefix in split form: pe holds p0 | p2 and po p1 | p3 in the high bytes of its halfwords
+    __device__ static __forceinline__ void prefix_split(uint32_t w, uint32_t& pe, uint32_t& po) {
+        const uint32_t e = w << 8;                   // high bytes b0 | b2
+        const uint32_t m = h(e, w);                  // high bytes op(b0,b1) | op(b2,b3)
+        const uint32_t s = (m << 16) | (ID * 0x0101u);
+        pe = h(e, s);
+        po = h(m, s);
+    }
+    __device__ static __forceinline__ uint32_t join(uint32_t pe, uint32_t po) { return __byte_perm(pe, po, 0x7351u); }
+    __device__ static __forceinline__ uint32_t prefix(uint32_t w) {
+        uint32_t pe, po;
+        prefix_split(w, pe, po);
+        return join(pe, po);
+    }
+    // chains a split prefix onto the split prefix before it (whose last element is po_prev's top byte)
+    __device__ static __forceinline__ void chain(uint32_t& pe, uint32_t& po, uint32_t po_prev) {
+        const uint32_t c = __byte_perm(po_prev, 0u, 0x3333u);
+        pe = h(pe, c);
+        po = h(po, c);
+    }
+    // op over the 16 bytes of r into the split accumulators (order does not matter for max / min)
+    __device__ static __forceinline__ void fold16(uint4 r, uint32_t& ae, uint32_t& ao) {
+        ao = h(ao, h(h(r.x, r.y), h(r.z, r.w)));
+        ae = h(ae, h(h(r.x << 8, r.y << 8), h(r.z << 8, r.w << 8)));
+    }
+    __device__ static __forceinline__ uint32_t fold_total(uint32_t ae, uint32_t ao) {
+        const uint32_t t = h(ae, ao);  // high bytes: the totals of the two halves
+        return h(t, t << 16) >> 24;
+    }
+};
+template <>
+struct Swar<int8_t, JMax> : SwarBytePair<int8_t, JMax, 0x80u> {};
+template <>
+struct Swar<int8_t, JMin> : SwarBytePair<int8_t, JMin, 0x7Fu> {};
+template <>
+struct Swar<uint8_t, JMax> : SwarBytePair<uint8_t, JMax, 0x00u> {};
+template <>
+struct Swar<uint8_t, JMin> : SwarBytePair<uint8_t, JMin, 0xFFu> {};
+#else
 template <>
 struct Swar<int8_t, JMax> : SwarBase<int8_t, JMax, 0x80u> {
     __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
@@ -382,6 +463,7 @@ template <>
 struct Swar<int8_t, JMin> : SwarBase<int8_t, JMin, 0x7Fu> {
     __device__ static __forceinline__ uint32_t comb(uint32_t a, uint32_t b) { return __vmins4(a, b); }
 };
+#endif
 #if KI_SWAR16_MAXMIN
 template <>
 struct Swar<int16_t, JMax> : SwarBase<int16_t, JMax, 0x8000u> {
@@ -409,9 +491,13 @@ constexpr bool swar_on() {
 // inclusive prefix of the element lanes of w (lowest lane first)
 template <class SW>
 __device__ __forceinline__ uint32_t swar_prefix(uint32_t w) {
+    if constexpr (SW::kOwnPrefix) {
+        return SW::prefix(w);
+    } else {
 #pragma unroll
-    for (int s = SW::kBits; s < 32; s <<= 1) w = SW::comb(w, (w << s) | (SW::kId & ((1u << s) - 1u)));
-    return w;
+        for (int s = SW::kBits; s < 32; s <<= 1) w = SW::comb(w, (w << s) | (SW::kId & ((1u << s) - 1u)));
+        return w;
+    }
 }
 
 }  // namespace ki

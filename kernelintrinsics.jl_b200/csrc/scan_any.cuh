@@ -217,15 +217,24 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             A s = id;
             if constexpr (ki::swar_on<T, Op>()) {
                 using SW = ki::Swar<T, Op>;
-                uint32_t acc = SW::kId;
+                if constexpr (SW::kSplit) {
+                    uint32_t ae = SW::kId, ao = SW::kId;
 #pragma unroll
-                for (int j = 0; j < S::kRows; ++j) {
-                    const uint4 r = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
-                    acc = SW::comb(acc, SW::comb(SW::comb(r.x, r.y), SW::comb(r.z, r.w)));
+                    for (int j = 0; j < S::kRows; ++j)
+                        SW::fold16(*reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane), ae, ao);
+                    s = (A)(T)SW::fold_total(ae, ao);
+                } else {
+                    uint32_t acc = SW::kId;
+#pragma unroll
+                    for (int j = 0; j < S::kRows; ++j) {
+                        const uint4 r = *reinterpret_cast<const uint4*>(sb + w * S::kSpan + S::kRow * j + kE * lane);
+                        acc = SW::comb(acc, SW::comb(SW::comb(r.x, r.y), SW::comb(r.z, r.w)));
+                    }
+#pragma unroll
+                    for (int sh = 16; sh >= SW::kBits; sh >>= 1)
+                        acc = SW::comb(acc, (acc >> sh) | (SW::kId & ~(0xFFFFFFFFu >> sh)));
+                    s = (A)(T)(acc & SW::kMask);
                 }
-#pragma unroll
-                for (int sh = 16; sh >= SW::kBits; sh >>= 1) acc = SW::comb(acc, (acc >> sh) | (SW::kId & ~(0xFFFFFFFFu >> sh)));
-                s = (A)(T)(acc & SW::kMask);
             } else {
 #pragma unroll
                 for (int j = 0; j < S::kRows; ++j) {
@@ -291,19 +300,42 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 // the way out (no per-element arrays: 16-byte lanes of 1-byte elements stay in registers)
                 if constexpr (ki::swar_on<T, Op>()) {
                     using SW = ki::Swar<T, Op>;
-                    uint32_t y0 = ki::swar_prefix<SW>(v[jj].raw.x), y1 = ki::swar_prefix<SW>(v[jj].raw.y);
-                    uint32_t y2 = ki::swar_prefix<SW>(v[jj].raw.z), y3 = ki::swar_prefix<SW>(v[jj].raw.w);
                     constexpr int kTop = 32 - SW::kBits;  // shift of a word's last element
-                    y1 = SW::comb(y1, SW::bcast(y0 >> kTop));
-                    y2 = SW::comb(y2, SW::bcast(y1 >> kTop));
-                    y3 = SW::comb(y3, SW::bcast(y2 >> kTop));
-                    const A tot = (A)(T)(y3 >> kTop);
-                    const A inc = ki::warpreduce(tot, op);
-                    A before = __shfl_up_sync(0xffffffffu, inc, 1);
-                    if (lane == 0) before = id;
-                    const A run = op(carry, before);
-                    const uint32_t rb = SW::bcast((uint32_t)(typename std::make_unsigned<T>::type)run);
-                    uint32_t o0 = SW::comb(y0, rb), o1 = SW::comb(y1, rb), o2 = SW::comb(y2, rb), o3 = SW::comb(y3, rb);
+                    uint32_t o0, o1, o2, o3, rb;
+                    A inc;
+                    if constexpr (SW::kSplit) {
+                        // byte max / min: the words stay split into even and odd bytes (the high bytes
+                        // of halfwords) until the running prefix is in, then are joined once
+                        uint32_t e0, d0, e1, d1, e2, d2, e3, d3;
+                        SW::prefix_split(v[jj].raw.x, e0, d0);
+                        SW::prefix_split(v[jj].raw.y, e1, d1);
+                        SW::prefix_split(v[jj].raw.z, e2, d2);
+                        SW::prefix_split(v[jj].raw.w, e3, d3);
+                        SW::chain(e1, d1, d0);
+                        SW::chain(e2, d2, d1);
+                        SW::chain(e3, d3, d2);
+                        inc = ki::warpreduce((A)(T)(d3 >> kTop), op);
+                        A before = __shfl_up_sync(0xffffffffu, inc, 1);
+                        if (lane == 0) before = id;
+                        const A run = op(carry, before);
+                        rb = SW::bcast((uint32_t)(typename std::make_unsigned<T>::type)run);
+                        o0 = SW::join(SW::h(e0, rb), SW::h(d0, rb));
+                        o1 = SW::join(SW::h(e1, rb), SW::h(d1, rb));
+                        o2 = SW::join(SW::h(e2, rb), SW::h(d2, rb));
+                        o3 = SW::join(SW::h(e3, rb), SW::h(d3, rb));
+                    } else {
+                        uint32_t y0 = ki::swar_prefix<SW>(v[jj].raw.x), y1 = ki::swar_prefix<SW>(v[jj].raw.y);
+                        uint32_t y2 = ki::swar_prefix<SW>(v[jj].raw.z), y3 = ki::swar_prefix<SW>(v[jj].raw.w);
+                        y1 = SW::comb(y1, SW::top(y0));
+                        y2 = SW::comb(y2, SW::top(y1));
+                        y3 = SW::comb(y3, SW::top(y2));
+                        inc = ki::warpreduce((A)(T)(y3 >> kTop), op);
+                        A before = __shfl_up_sync(0xffffffffu, inc, 1);
+                        if (lane == 0) before = id;
+                        const A run = op(carry, before);
+                        rb = SW::bcast((uint32_t)(typename std::make_unsigned<T>::type)run);
+                        o0 = SW::comb(y0, rb), o1 = SW::comb(y1, rb), o2 = SW::comb(y2, rb), o3 = SW::comb(y3, rb);
+                    }
                     if (EXCL) {  // shift by one element: the first is the running prefix
                         o3 = (o3 << SW::kBits) | (o2 >> kTop);
                         o2 = (o2 << SW::kBits) | (o1 >> kTop);

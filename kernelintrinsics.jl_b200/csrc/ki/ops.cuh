@@ -375,6 +375,10 @@ struct SwarBase {
     __device__ static __forceinline__ uint32_t top(uint32_t w) {
         return __byte_perm(w, 0u, sizeof(T) == 1 ? 0x3333u : 0x3232u);
     }
+    // element lane r of w in every lane
+    __device__ static __forceinline__ uint32_t spread(uint32_t w, int r) {
+        return __byte_perm(w, 0u, sizeof(T) == 1 ? 0x1111u * (uint32_t)r : (r ? 0x3232u : 0x1010u));
+    }
 };
 template <class T>
 struct Swar<T, JOr> : SwarBase<T, JOr, 0x00u> {

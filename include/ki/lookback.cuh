@@ -151,7 +151,8 @@ __device__ __forceinline__ int64_t decoupled_lookback(TileStatus st, uint64_t t,
 // 8-byte integers when their two's-complement value fits 61 bits (bits 3-63).  Anything else
 // (every Float64, large 64-bit integers) lives in the side arrays (aggs for aggregates, incls for
 // inclusive prefixes, as raw bits) with the wide bit set in its status word; a fence.acq_rel.gpu
-// orders those value loads after the status loads.  `op` must be associative and commutative
+// orders those value loads after the status loads.  With PAIR every value rides in two status words
+// instead (publish_any), so a window is one round trip to L2 for any 8-byte value.  `op` must be associative and commutative
 // (Base + on integers, max, min; Float64 + up to rounding).
 // ---------------------------------------------------------------------------------------------
 template <class A>
@@ -194,8 +195,19 @@ __device__ __forceinline__ A unpack_value(uint64_t w) {
     else return from_bits<A>((uint64_t)((int64_t)w >> 3));
 }
 
-template <bool LOSSY = false, class A>
+// PAIR: an 8-byte value rides in two status words, words[2t] (its high 32 bits) and words[2t + 1]
+// (its low 32 bits), each beside the state; a tile's states only move none -> aggregate -> prefix
+// and each state has one value, so two words that show the same state hold one value, and a pair
+// caught between two publishes (states differ) reads as not ready.  No side arrays, no fence.
+template <bool LOSSY = false, bool PAIR = false, class A>
 __device__ __forceinline__ void publish_any(TileStatus st, uint64_t t, uint64_t state, A v) {
+    if constexpr (PAIR) {
+        static_assert(sizeof(A) == 8, "word pairs carry 8-byte values");
+        const uint64_t b = to_bits(v);
+        store<Order::Release, Scope::Device>(&st.words[2 * t], (uint64_t)((b & 0xFFFFFFFF00000000ull) | state));
+        store<Order::Release, Scope::Device>(&st.words[2 * t + 1], (uint64_t)((b << 32) | state));
+        return;
+    }
     uint64_t packed;
     if (pack_value<LOSSY>(v, packed)) {
         store<Order::Release, Scope::Device>(&st.words[t], packed | state);
@@ -208,20 +220,20 @@ __device__ __forceinline__ void publish_any(TileStatus st, uint64_t t, uint64_t 
 
 // head: tile t starts a segment (tile 0, or the first tile of a row in a segmented scan); its
 // inclusive prefix is op(init, agg) at once, and no lookback passes it.
-template <bool LOSSY = false, class A, class F>
+template <bool LOSSY = false, bool PAIR = false, class A, class F>
 __device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op, bool head) {
-    if (head) publish_any<LOSSY>(st, t, kFlagPrefix, op(init, agg));
-    else publish_any<LOSSY>(st, t, kFlagAgg, agg);
+    if (head) publish_any<LOSSY, PAIR>(st, t, kFlagPrefix, op(init, agg));
+    else publish_any<LOSSY, PAIR>(st, t, kFlagAgg, agg);
 }
-template <bool LOSSY = false, class A, class F>
+template <bool LOSSY = false, bool PAIR = false, class A, class F>
 __device__ __forceinline__ void publish_aggregate_any(TileStatus st, uint64_t t, A agg, A init, F op) {
-    publish_aggregate_any<LOSSY>(st, t, agg, init, op, t == 0);
+    publish_aggregate_any<LOSSY, PAIR>(st, t, agg, init, op, t == 0);
 }
 
 // Run by all 32 lanes of one warp after publish_aggregate_any(t).  Returns the exclusive prefix of
 // tile t (init for a head tile) and publishes tile t's inclusive prefix.  The walk stops at the
 // nearest inclusive prefix, so it never crosses a head tile into an earlier segment.
-template <int K, bool LOSSY = false, class A, class F>
+template <int K, bool LOSSY = false, bool PAIR = false, class A, class F>
 __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
                                                     uint32_t* status, uint64_t timeout_ns, bool head) {
     const unsigned lane = lane0();
@@ -234,14 +246,24 @@ __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A
     const uint64_t* aggs = reinterpret_cast<const uint64_t*>(st.aggs);
     const uint64_t* incls = reinterpret_cast<const uint64_t*>(st.incls);
     while (true) {
-        uint64_t w[K];
+        uint64_t w[K], lo[K];
         int first_p, first_zero;
         int pos_p, pos_zero;
         while (true) {
 #pragma unroll
             for (int k = 0; k < K; ++k) {
                 const long long idx = end - (long long)(lane * K + k);
-                w[k] = (idx >= 0) ? load<Order::Relaxed, Scope::Device>(&st.words[idx]) : kFlagPrefix;
+                if constexpr (PAIR) {
+                    w[k] = kFlagPrefix;
+                    lo[k] = 0;
+                    if (idx >= 0) {
+                        w[k] = load<Order::Relaxed, Scope::Device>(&st.words[2 * idx]);
+                        lo[k] = load<Order::Relaxed, Scope::Device>(&st.words[2 * idx + 1]);
+                        if ((w[k] & 3) != (lo[k] & 3)) w[k] = kFlagNone;  // between two publishes
+                    }
+                } else {
+                    w[k] = (idx >= 0) ? load<Order::Relaxed, Scope::Device>(&st.words[idx]) : kFlagPrefix;
+                }
             }
             first_p = K;
             first_zero = K;
@@ -274,7 +296,8 @@ __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A
         for (int k = 0; k < K; ++k) {
             const int p = (int)lane * K + k;
             if (p <= pos_p && p < 32 * K && end - p >= 0) {
-                if (w[k] & kFlagWide) any_wide = true;
+                if constexpr (PAIR) v = op(v, from_bits<A>((w[k] & 0xFFFFFFFF00000000ull) | (lo[k] >> 32)));
+                else if (w[k] & kFlagWide) any_wide = true;
                 else v = op(v, unpack_value<A, LOSSY>(w[k]));
             }
         }
@@ -295,13 +318,13 @@ __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A
         if (pos_p < 32 * K) break;
         end -= 32 * K;
     }
-    if (lane == 0) publish_any<LOSSY>(st, t, kFlagPrefix, op(excl, agg));
+    if (lane == 0) publish_any<LOSSY, PAIR>(st, t, kFlagPrefix, op(excl, agg));
     return excl;
 }
-template <int K, bool LOSSY = false, class A, class F>
+template <int K, bool LOSSY = false, bool PAIR = false, class A, class F>
 __device__ __forceinline__ A decoupled_lookback_any(TileStatus st, uint64_t t, A agg, A init, A identity, F op,
                                                     uint32_t* status, uint64_t timeout_ns) {
-    return decoupled_lookback_any<K, LOSSY>(st, t, agg, init, identity, op, status, timeout_ns, t == 0);
+    return decoupled_lookback_any<K, LOSSY, PAIR>(st, t, agg, init, identity, op, status, timeout_ns, t == 0);
 }
 
 // ---------------------------------------------------------------------------------------------

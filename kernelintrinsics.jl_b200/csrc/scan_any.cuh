@@ -58,6 +58,29 @@ constexpr int kThreads = kWorkThreads + 32;
 #ifndef KI_SCAN_ANY_PACK_TOTALS
 #define KI_SCAN_ANY_PACK_TOTALS 1
 #endif
+// How tile values ride in the status words (ki/lookback.cuh).  Float32 sums and products accumulate
+// in Float64 and are rounded to Float32 on output: one word, 3 mantissa bits dropped.  Everything
+// else: one word when the value fits (the side arrays behind a fence otherwise).
+// KI_SCAN_ANY_PAIR=1 puts 8-byte values other than integer sums in word pairs instead (no side
+// arrays, no fence, two loads per tile and window).  Measured at 2^27 (fraction of the copy peak,
+// one word -> pairs): Float64 cumsum 0.70 -> 0.71, Float64 cumprod 0.70 -> 0.71, Int64 xor of random
+// values 0.68 -> 0.70, but where the values mostly fit 61 bits the second load costs: UInt64 | 0.79
+// -> 0.70, Int64 cumprod 0.69 -> 0.63, Int32 cumprod into Int64 0.73 -> 0.69.  The Float64 scans are
+// not held back by their lookback, so pairs stay off.
+#ifndef KI_SCAN_ANY_PAIR
+#define KI_SCAN_ANY_PAIR 0
+#endif
+template <class T, class Op>
+constexpr bool status_lossy() {
+    using A = typename ki::Traits<T, Op>::A;
+    return KI_SCAN_ANY_PACK_F32 && std::is_same<T, float>::value && std::is_same<A, double>::value;
+}
+template <class T, class Op>
+constexpr bool status_pair() {
+    using A = typename ki::Traits<T, Op>::A;
+    return KI_SCAN_ANY_PAIR && sizeof(A) == 8 && !status_lossy<T, Op>() &&
+           !(std::is_integral<A>::value && std::is_same<Op, ki::JAdd>::value);
+}
 #ifndef KI_SCAN_ANY_ROWS_2B
 #define KI_SCAN_ANY_ROWS_2B 8
 #endif
@@ -158,9 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
     using R = typename Tr::R;
     using S = Shape<T>;
     constexpr int kE = S::kE;
-    // Float32 sums and products accumulate in Float64 and are rounded to Float32 on output: their
-    // tile values ride in the status words with 3 mantissa bits dropped (no side-array round trips)
-    constexpr bool kLossy = KI_SCAN_ANY_PACK_F32 && std::is_same<T, float>::value && std::is_same<A, double>::value;
+    constexpr bool kLossy = status_lossy<T, Op>();
+    constexpr bool kPair = status_pair<T, Op>();
     const ki::OpFn<T, Op> op;
     const A id = Tr::identity();
     const A init = ki::from_bits<A>(a.init_bits);
@@ -225,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
         if (w == kLookWarp) {
             if (have_old) {
                 PendingAny<A>& o = slot[cur ^ 1];
-                const A ex = ki::decoupled_lookback_any<1, kLossy>(a.st, o.t, o.agg, init, id, op, a.status,
+                const A ex = ki::decoupled_lookback_any<1, kLossy, kPair>(a.st, o.t, o.agg, init, id, op, a.status,
                                                                    a.timeout_ns, where(o.t).head);
                 if (lane == 0) o.tile_excl = ex;
             }
@@ -286,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 if (lane == 0) {
                     e.t = t_new;
                     e.agg = agg;
-                    ki::publish_aggregate_any<kLossy>(a.st, t_new, agg, init, op, p.head);
+                    ki::publish_aggregate_any<kLossy, kPair>(a.st, t_new, agg, init, op, p.head);
                 }
             }
         }
@@ -687,7 +709,9 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, const Sca
     int rc = ki::ensure_region(ctx, KI_REG_SCAN_ANY, words_off + ntiles * 24, &base);
     if (rc) return rc;
     char* b = static_cast<char*>(base);
-    KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * sizeof(uint64_t), s));
+    // status words: one per tile, or two per tile when values ride in pairs (the region's next 8
+    // bytes per tile, otherwise the aggregates' side array)
+    KI_CUDA(ctx, cudaMemsetAsync(b, 0, words_off + ntiles * (status_pair<T, Op>() ? 16 : 8), s));
     AnyArgs a;
     a.in = d_in;
     a.out = d_out;

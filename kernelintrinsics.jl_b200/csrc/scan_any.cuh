@@ -70,6 +70,24 @@ constexpr int kThreads = kWorkThreads + 32;
 #ifndef KI_SCAN_ANY_PAIR
 #define KI_SCAN_ANY_PAIR 0
 #endif
+#ifndef KI_SCAN_ANY_INVERSE
+#define KI_SCAN_ANY_INVERSE 1
+#endif
+// Operators whose lanes' exclusive prefix follows from the inclusive one and the lane's own total
+// exactly (wrapping integer +, xor): no shuffle for it.  At 2^27 (fraction of the copy peak, with
+// the shuffle -> without): UInt8 cumsum into UInt64 0.74 -> 0.77, Int64 + of values beyond 61 bits
+// 0.706 -> 0.717, Int32 xor 0.846 -> 0.855, Int32 cumsum into Int64 0.81 -> 0.80; results identical.
+template <class A, class Op>
+constexpr bool has_inverse() {
+    return KI_SCAN_ANY_INVERSE && std::is_integral<A>::value &&
+           (std::is_same<Op, ki::JAdd>::value || std::is_same<Op, ki::JXor>::value);
+}
+template <class Op, class A>
+__device__ __forceinline__ A exclusive_from(A inc, A tot) {
+    using U = typename std::make_unsigned<A>::type;
+    if constexpr (std::is_same<Op, ki::JXor>::value) return (A)((U)inc ^ (U)tot);
+    else return (A)((U)inc - (U)tot);
+}
 template <class T, class Op>
 constexpr bool status_lossy() {
     using A = typename ki::Traits<T, Op>::A;
@@ -465,8 +483,13 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
 #pragma unroll
                 for (int e = 1; e < kE; ++e) tot = op(tot, Tr::lift(v[jj].get(e)));
                 const A inc = ki::warpreduce(tot, op);
-                A before = __shfl_up_sync(0xffffffffu, inc, 1);
-                if (lane == 0) before = id;
+                A before;
+                if constexpr (has_inverse<A, Op>()) {
+                    before = exclusive_from<Op>(inc, tot);
+                } else {
+                    before = __shfl_up_sync(0xffffffffu, inc, 1);
+                    if (lane == 0) before = id;
+                }
                 A run = op(carry, before);
                 const int i = w * S::kSpan + S::kRow * j + kE * (int)lane;
                 if constexpr (Stage<T, Op>::kOn) {

@@ -84,7 +84,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="", help="comma list of kernels to run under 'kernels'")
     p.add_argument("--profile", default="", choices=["", "copy", "reduce", "scan", "compact", "gemm", "scan_f32", "scan_u8", "rows", "copy2d",
-                            "count"],
+                            "count", "scan_i8max", "scan_u8or"],
                    help="run only this kernel, --profile-launches times, on a small case (for ncu)")
     p.add_argument("--profile-n", type=int, default=0, help="elements (bytes for copy; M=N=K for gemm)")
     p.add_argument("--profile-launches", type=int, default=3)
@@ -145,6 +145,16 @@ def run_profile(args):
         y = torch.empty(n, dtype=torch.uint64, device=dev)
         fn = lambda: KI.scan(x, "+", out=y)
         alg = 9 * n
+    elif k in ("scan_i8max", "scan_u8or"):
+        n = n or (1 << 27)  # accumulate(max) over Int8 / accumulate(|) over UInt8, same type out
+        x = torch.empty(n, dtype=torch.uint8, device=dev)
+        KI.fill_bytes(x, seed=2)
+        if k == "scan_i8max":
+            x = x.view(torch.int8)
+        y = torch.empty_like(x)
+        op = "max" if k == "scan_i8max" else "|"
+        fn = lambda: KI.scan(x, op, out=y)
+        alg = 2 * n
     elif k == "copy2d":
         n = n or 8192  # rows of 32 KiB between pitches 33000 and 40000, odd offsets
         src = torch.empty(n * 33000 + 16, dtype=torch.uint8, device=dev)

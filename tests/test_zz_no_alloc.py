@@ -44,6 +44,44 @@ def test_noalloc_scan_matches_oracle_and_context_scan_twice(KI, dev, oracle):
         assert torch.equal(got, want_ctx), n
 
 
+def test_noalloc_scan_inside_a_cuda_graph(KI, dev, oracle):
+    """The use it was built for: after one warm-up call (the one-time set-up runs outside capture),
+    the call is captured into a CUDA graph under torch's global capture mode, which refuses any
+    allocation, and the graph is replayed on new data twice, each replay equal to the oracle and to
+    the context scan."""
+    import torch
+
+    from kernelintrinsics import _abi
+
+    lib = _abi.load()
+    n = (1 << 21) + 77
+    seed = -31
+    x = torch.empty(n, dtype=torch.int64, device=dev)
+    KI.fill_int_range(x, seed=13, lo=-1000, hi=1000)
+    y = torch.empty_like(x)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        assert _noalloc(lib, x, y, n, seed, side) == _abi.KI_OK
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    rcs = []
+    with torch.cuda.graph(g):
+        rcs.append(_noalloc(lib, x, y, n, seed, torch.cuda.current_stream(dev)))
+    assert rcs == [_abi.KI_OK]
+    for data_seed in (29, 41):
+        KI.fill_int_range(x, seed=data_seed, lo=-1000, hi=1000)
+        y.fill_(7)
+        g.replay()
+        torch.cuda.synchronize()
+        want = oracle.cumsum_i64(oracle.gen_int_range_i64(data_seed, -1000, 1000, n), seed=seed)
+        assert np.array_equal(y.cpu().numpy(), want), data_seed
+        assert torch.equal(y, KI.warpreduce_scan(x, seed=seed)), data_seed
+    del g
+    torch.cuda.synchronize()
+
+
 def test_noalloc_scan_at_its_largest_size(KI, dev):
     """n just under the maximum fills nearly every tile slot of the static scratch; the output is
     fixed exactly by out[0] = seed + in[0] and out[i] - out[i-1] = in[i] (checked on the device)."""

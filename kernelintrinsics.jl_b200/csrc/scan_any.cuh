@@ -49,6 +49,10 @@ constexpr int kThreads = kWorkThreads + 32;
 // Two 16-byte vectors per lane and step for 4- and 8-byte elements (one warp scan per 2*kE
 // elements a lane, lanes 32 bytes apart) was slower everywhere at 2^28: Float32 cumsum 0.76 -> 0.66,
 // Int32 -> Int64 cumsum 0.84 -> 0.68, Float64 cumsum 0.72 -> 0.69, Int32 xor 0.89 -> 0.81.
+// Lane-wise (SWAR) scans load all 8 rows of a warp's span before scanning them.  With the packed
+// lane totals that spills 16-36 bytes in the 1-byte instances; loading 4 rows at a time removes
+// most of it but is slower (UInt8 | 0.646 -> 0.638, Int8 max 0.571 -> 0.547, Int16 | 0.846 ->
+// 0.798, Int16 max 0.846 -> 0.776): the loads in flight matter more than the spills.
 #ifndef KI_SCAN_ANY_SWAR_ALLROWS
 #define KI_SCAN_ANY_SWAR_ALLROWS 1
 #endif

@@ -77,6 +77,29 @@ constexpr int kThreads = kWorkThreads + 32;
 #ifndef KI_SCAN_ANY_INVERSE
 #define KI_SCAN_ANY_INVERSE 1
 #endif
+#ifndef KI_SCAN_ANY_IDEMPOTENT
+#define KI_SCAN_ANY_IDEMPOTENT 1
+#endif
+template <class Op>
+constexpr bool idempotent() {
+    return KI_SCAN_ANY_IDEMPOTENT && (std::is_same<Op, ki::JMax>::value || std::is_same<Op, ki::JMin>::value ||
+                                      std::is_same<Op, ki::JOr>::value || std::is_same<Op, ki::JAnd>::value);
+}
+// Inclusive warp scan (ki::warpreduce).  For idempotent operators no lane test is needed: where the
+// source lane would be below lane 0, __shfl_up_sync returns the caller's own value, and op(v, v) = v.
+// At 2^28 (fraction of the copy peak, with the lane test -> without): Float32 accumulate(max) 0.623
+// -> 0.672, (min) 0.622 -> 0.669, Float64 max 0.515 -> 0.532, Int8 max 0.571 -> 0.581, UInt8 | 0.634
+// -> 0.649; Int32 max and & and Int16 max unchanged (0.84-0.90); results identical.
+template <class Op, class A, class F>
+__device__ __forceinline__ A warp_scan(A v, F op) {
+    if constexpr (idempotent<Op>()) {
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) v = op(ki::shfl<ki::Dir::Up>(v, off), v);
+        return v;
+    } else {
+        return ki::warpreduce(v, op);
+    }
+}
 // Operators whose lanes' exclusive prefix follows from the inclusive one and the lane's own total
 // exactly (wrapping integer +, xor): no shuffle for it.  At 2^27 (fraction of the copy peak, with
 // the shuffle -> without): UInt8 cumsum into UInt64 0.74 -> 0.77, Int64 + of values beyond 61 bits
@@ -321,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
             work_sync();
             if (w == 0) {
                 const A x = (lane < (unsigned)kWorkWarps) ? warp_tot[lane] : id;
-                const A inc = ki::warpreduce(x, op);
+                const A inc = warp_scan<Op>(x, op);
                 A exc = __shfl_up_sync(0xffffffffu, inc, 1);
                 if (lane == 0) exc = id;
                 const A agg = __shfl_sync(0xffffffffu, inc, kWorkWarps - 1);
@@ -407,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
 #pragma unroll
                     for (int off = 1; off < 32; off <<= 1) {
                         const uint32_t x = __shfl_up_sync(0xffffffffu, inc, off);
-                        if ((int)lane >= off) inc = SW::comb(x, inc);
+                        if (idempotent<Op>() || (int)lane >= off) inc = SW::comb(x, inc);
                     }
                     uint32_t before = __shfl_up_sync(0xffffffffu, inc, 1);
                     if (lane == 0) before = SW::kId;
@@ -456,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                         SW::chain(e1, d1, d0);
                         SW::chain(e2, d2, d1);
                         SW::chain(e3, d3, d2);
-                        inc = ki::warpreduce((A)(T)(d3 >> kTop), op);
+                        inc = warp_scan<Op>((A)(T)(d3 >> kTop), op);
                         A before = __shfl_up_sync(0xffffffffu, inc, 1);
                         if (lane == 0) before = id;
                         const A run = op(carry, before);
@@ -471,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                         y1 = SW::comb(y1, SW::top(y0));
                         y2 = SW::comb(y2, SW::top(y1));
                         y3 = SW::comb(y3, SW::top(y2));
-                        inc = ki::warpreduce((A)(T)(y3 >> kTop), op);
+                        inc = warp_scan<Op>((A)(T)(y3 >> kTop), op);
                         A before = __shfl_up_sync(0xffffffffu, inc, 1);
                         if (lane == 0) before = id;
                         const A run = op(carry, before);
@@ -486,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
                 A tot = Tr::lift(v[jj].get(0));
 #pragma unroll
                 for (int e = 1; e < kE; ++e) tot = op(tot, Tr::lift(v[jj].get(e)));
-                const A inc = ki::warpreduce(tot, op);
+                const A inc = warp_scan<Op>(tot, op);
                 A before;
                 if constexpr (has_inverse<A, Op>()) {
                     before = exclusive_from<Op>(inc, tot);
@@ -626,7 +649,7 @@ __global__ void __launch_bounds__(kRowThreads) scan_rows_warp_kernel(const T* __
             A tot = Tr::lift(v.get(0));
 #pragma unroll
             for (int e = 1; e < kE; ++e) tot = op(tot, Tr::lift(v.get(e)));
-            const A inc = ki::warpreduce(tot, op);
+            const A inc = warp_scan<Op>(tot, op);
             A before = __shfl_up_sync(0xffffffffu, inc, 1);
             if (lane == 0) before = id;
             A run = op(carry, before);

@@ -409,7 +409,7 @@ int ki_comm_init_rank(int device, int nranks, int rank, const ki_comm_id* id, in
         cfg.blocking = 0;  // set-up waits are bounded on the host (nccl_wait)
         rc = nccl_wait(c, N->CommInitRankConfig(&c->nc, nranks, u, rank, &cfg), "ncclCommInitRankConfig");
     }
-    // round 1: exchange buffers and GPU identities
+    // step 1: exchange buffers and GPU identities
     RankRecord mine;
     memset(&mine, 0, sizeof(mine));
     std::vector<RankRecord> all;
@@ -431,7 +431,7 @@ int ki_comm_init_rank(int device, int nranks, int rank, const ki_comm_id* id, in
                                        "ranks %d and %d share one GPU: their exchange waits would wait on one another",
                                        i, j);
     }
-    // round 2: map every peer's buffer; all ranks agree on peer or NCCL exchange
+    // step 2: map every peer's buffer; all ranks agree on peer or NCCL exchange
     std::vector<XSlot*> bufs(nranks, nullptr);
     if (!rc) {
         int ok = exchange != KI_XCHG_NCCL;

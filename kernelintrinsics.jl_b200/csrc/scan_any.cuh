@@ -168,6 +168,16 @@ struct Stage {
     }
 };
 
+// The identity the scan folds from.  For Float64 accumulation of + it is -0.0 (-0.0 + x is x for
+// every x, while +0.0 + -0.0 is +0.0), so sums over negative zeros keep their sign as Base.cumsum's
+// do; the other operators take their traits' identity.
+template <class T, class Op>
+__device__ __forceinline__ typename ki::Traits<T, Op>::A scan_identity() {
+    using A = typename ki::Traits<T, Op>::A;
+    if constexpr (std::is_floating_point<A>::value && std::is_same<Op, ki::JAdd>::value) return A(-0.0);
+    else return ki::Traits<T, Op>::identity();
+}
+
 // One row of a lane-wise (SWAR) scan on its way out: the lane's four result words o0..o3, shifted
 // by one element for an exclusive scan (the first element is then the running prefix, rb's lowest
 // element), stored as one 16-byte vector when the tile is full and the output aligned, else element
@@ -229,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) scan_any_kernel(AnyArgs a) {
     constexpr bool kLossy = status_lossy<T, Op>();
     constexpr bool kPair = status_pair<T, Op>();
     const ki::OpFn<T, Op> op;
-    const A id = Tr::identity();
+    const A id = scan_identity<T, Op>();
     const A init = ki::from_bits<A>(a.init_bits);
     const T* in = static_cast<const T*>(a.in);
     R* out = static_cast<R*>(a.out);
@@ -622,7 +632,7 @@ __global__ void __launch_bounds__(kRowThreads) scan_rows_warp_kernel(const T* __
     constexpr int kE = (int)(16 / sizeof(T));
     constexpr int kRow = 32 * kE;
     const ki::OpFn<T, Op> op;
-    const A id = Tr::identity();
+    const A id = scan_identity<T, Op>();
     const A init = ki::from_bits<A>(init_bits);
     const T pad = ki::pad_value<T, Op>();
     const unsigned lane = threadIdx.x & 31;
@@ -733,7 +743,11 @@ int scan_launch(ki_ctx* ctx, bool excl, const void* d_in, void* d_out, const Sca
     const bool in_place = i0 == o0 && sizeof(T) == sizeof(R) && ld_in == ld_out;
     if (!in_place && i0 < o0 + ob && o0 < i0 + ib)
         return ki::set_error(ctx, KI_ERR_ARG, "scan: input and output overlap (only an exact in-place scan is allowed)");
-    const A init = init_value<T, Op>(h_init);
+    A init = init_value<T, Op>(h_init);
+    // an inclusive float cumsum without init starts from -0.0, the identity: out[1] is x[1], sign
+    // included (an exclusive one writes its init, +0.0, first)
+    if constexpr (std::is_floating_point<A>::value && std::is_same<Op, ki::JAdd>::value)
+        if (!h_init && !excl) init = A(-0.0);
     uint64_t init_bits = 0;
     memcpy(&init_bits, &init, sizeof(A));
     const int vec_in = ki::aligned(d_in, 16) && (rows == 1 || (ld_in * sizeof(T)) % 16 == 0);

@@ -109,6 +109,25 @@ def test_scan_init_misaligned_and_in_place(KI, oracle, dev, dt):
     KI.context(0).check()
 
 
+@pytest.mark.parametrize("dt", [np.float32, np.float64], ids=lambda d: np.dtype(d).name)
+def test_cumsum_keeps_negative_zeros(KI, oracle, dev, dt):
+    """Base.cumsum over negative zeros gives negative zeros (the first output is x[1], sign included):
+    bit-exact against the oracle, for plain scans of one to many tiles and for short and long rows."""
+    for n in (5, 40000, 300001):
+        x = np.full(n, -0.0, dtype=dt)
+        x[n // 2] = 1.5
+        got = KI.scan(_to_dev(x, dev), "+").cpu().numpy()
+        want = oracle.accumulate("+", x).astype(got.dtype)
+        assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), n
+    for rows, cols in ((6, 1000), (3, 100_003)):
+        m = np.full((rows, cols), -0.0, dtype=dt)
+        m[1, cols // 3] = 2.0
+        got = KI.scan_rows(_to_dev(m.reshape(-1), dev).view(rows, cols), "+").cpu().numpy()
+        want = np.stack([oracle.accumulate("+", m[r]) for r in range(rows)]).astype(got.dtype)
+        assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (rows, cols)
+    KI.context(0).check()
+
+
 @pytest.mark.parametrize("dt", [np.int8, np.uint8, np.int16, np.uint16], ids=lambda d: np.dtype(d).name)
 def test_scan_narrow_same_type_misaligned(KI, oracle, dev, dt):
     """1- and 2-byte scans that keep their type (lane-wise words inside the kernel) from inputs and

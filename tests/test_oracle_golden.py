@@ -182,6 +182,19 @@ def test_accumulate_matches_scalar_base_semantics(oracle):
     assert oracle.reduce_op("+", np.zeros(0, dtype=np.int32)) == 0
 
 
+def test_float_sums_keep_negative_zeros(oracle):
+    """Base: cumsum([-0.0, -0.0]) == [-0.0, -0.0] and sum([-0.0, -0.0]) === -0.0 (the first element starts
+    the fold, no +0.0 is added), while the sum of an empty collection is +0.0 (zero(T))."""
+    for dt in (np.float32, np.float64):
+        z = np.full(7, -0.0, dtype=dt)
+        assert np.signbit(oracle.accumulate("+", z)).all()
+        assert np.signbit(oracle.reduce_op("+", z))
+        mixed = oracle.accumulate("+", np.array([-0.0, -0.0, 2.0, -0.0], dtype=dt))
+        assert np.signbit(mixed).tolist() == [True, True, False, False]
+        empty = oracle.reduce_op("+", np.zeros(0, dtype=dt))
+        assert empty == 0 and not np.signbit(empty)
+
+
 def test_accumulate_products_bitwise_and_small_integers(oracle):
     """cumprod / accumulate(|, &, xor) and the widening of Int8/Int16/UInt8/UInt16 (Base.add_sum and
     Base.mul_prod widen them to 64 bits; the bitwise operators keep the type), against scalar loops
